@@ -1,0 +1,370 @@
+#!/usr/bin/env python
+"""Benchmark of the fused flow-matching sampler (one JSON line on rank 0).
+
+Headline metric: ms per 10-step sampler call at batch 1, on the action expert
+with d_model 1024, 4 blocks, 16 heads x 64, MLP 4096, prefix 256, horizon 50,
+action dim 32 (synthetic seeded weights and inputs), int4 group-128 weights,
+bf16 activations. A "step" of this benchmark is one sampler call (10 Euler
+steps). ``value`` is device time per call with inputs resident in HBM and the
+L2 flushed between calls; ``e2e`` is the same call through ``GraphedSampler``
+with the input in pinned host memory and the result copied back to the host
+inside the timed region. bf16 and int8 weights are reported beside int4, and
+the standalone dequant-GEMM's HBM throughput for the K=N=4096 sweep points.
+
+Multi-GPU (torchrun, one rank per GPU): independent replicas of the batch-1
+call (the call does not shard); ``value`` is the job's time per call
+(max-over-ranks device time / calls of all ranks), ``scaling`` "weak".
+
+``--impl reference`` times the CPU restatement of the reference's own path
+(the oracle: dequantise-then-matmul + eager Euler loop in torch on the host
+cores, all threads) on the same workload and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+WORKLOAD = dict(d_model=1024, n_layers=4, n_heads=16, horizon=50, action_dim=32, prefix_len=256,
+                mlp_ratio=4.0)
+METRIC = "ms per 10-step sampler call (batch 1)"
+N_STEPS = 10
+L2_FLUSH_BYTES = 256 << 20
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def linear_bytes(n, k, bits, group=128):
+    """Algorithmic bytes of one linear: weights + fp16-counted scales + bias
+    (the reference's accounting, kernel/quant.py:58-59)."""
+    if bits == 16:
+        return n * k * 2 + n * 2
+    return n * k * bits // 8 + n * (k // group) * 2 + n * 2
+
+
+def step_bytes(cfg, bits, batch=1):
+    """Bytes one Euler step must read: every per-step linear (t_proj, the six
+    block linears, dense in/out projections), norm parameters; plus the cached
+    prefix K/V separately."""
+    d, hid, a = cfg["d_model"], int(cfg["d_model"] * cfg["mlp_ratio"]), cfg["action_dim"]
+    w = linear_bytes(d, d, bits) + linear_bytes(d, a, 16) + linear_bytes(a, d, 16)
+    per_block = (linear_bytes(3 * d, d, bits) + linear_bytes(d, d, bits) * 3
+                 + linear_bytes(hid, d, bits) + linear_bytes(d, hid, bits) + 3 * 2 * d * 2)
+    w += cfg["n_layers"] * per_block + 2 * d * 2
+    kv = cfg["n_layers"] * 2 * batch * cfg["prefix_len"] * d * 2
+    return w, kv
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(backend):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return rank, world, local
+
+
+def build_expert(bits, device):
+    from embodied_efficiency_b200 import ActionExpert, ActionExpertConfig, quantize_model_triton, synth
+    cfg = ActionExpertConfig(**WORKLOAD)
+    params, x0, prefix = synth.workload(cfg, seed=0, batch=1)
+    m = ActionExpert(cfg)
+    m.load_state_dict(params)
+    m = m.to(device).bfloat16().eval()
+    if bits != 16:
+        quantize_model_triton(m, bits=bits)
+    return m, x0, prefix
+
+
+def time_calls(fn, steps, warmup, flush):
+    """Per-call device time (CUDA events on the launching stream), L2 flushed
+    between calls; returns the list of per-call ms."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record()
+        fn()
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in ev]
+
+
+def gemm_sweep(device, flush):
+    """Standalone dequant-GEMM at K=N=4096: algorithmic HBM GB/s per launch."""
+    from embodied_efficiency_b200 import wq_linear
+    from embodied_efficiency_b200.quant import quantize_weight
+    from embodied_efficiency_b200.wq_gemm import _pack_int4
+    out = {}
+    k = n = 4096
+    g = torch.Generator(device="cpu").manual_seed(0)
+    w = torch.randn(n, k, generator=g) * 0.02
+    mats = {16: (w.bfloat16().to(device), None)}
+    for bits in (8, 4):
+        q, s, gs = quantize_weight(w, bits, 128)
+        q2 = q.reshape(n, k).to(device)
+        mats[bits] = (_pack_int4(q2) if bits == 4 else q2, s.reshape(n, -1).to(device))
+    for m in (1, 16, 50):
+        x = torch.randn(m, k, generator=g).bfloat16().to(device)
+        for bits, (wt, sc) in mats.items():
+            ms = time_calls(lambda: wq_linear(x, wt, sc, None, 128, bits), 50, 5, flush)
+            t = statistics.median(ms)
+            nbytes = linear_bytes(n, k, bits) - n * 2 + m * k * 2 + m * n * 2
+            out[f"m{m}_{'bf16' if bits == 16 else f'int{bits}'}"] = {
+                "us": round(t * 1e3, 2), "GBps": round(nbytes / (t * 1e-3) / 1e9, 1)}
+    return out
+
+
+def cpu_baseline_run(budget_s=15.0, bits=4):
+    """The oracle (CPU restatement of the reference path) on the host cores."""
+    from embodied_efficiency_b200 import synth
+    from oracle import sampler as OS
+    cfg = OS.Cfg(**WORKLOAD)
+    params, x0, prefix = synth.workload(cfg, seed=0, batch=1)
+    p = {k: v.bfloat16() for k, v in params.items()}
+    qp = OS.quantize_params(p, cfg, bits) if bits != 16 else None
+    kv = OS.encode_prefix(p, cfg, prefix.bfloat16(), qp)
+    xb = x0.bfloat16()
+    OS.flow_sample(p, cfg, xb, N_STEPS, kv, qp)  # warm-up
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 2:
+        t0 = time.perf_counter()
+        OS.flow_sample(p, cfg, xb, N_STEPS, kv, qp)
+        times.append((time.perf_counter() - t0) * 1e3)
+    return statistics.median(times), len(times)
+
+
+def run_reference(args):
+    rank, world, _ = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), 0
+    if rank != 0:
+        return
+    from embodied_efficiency_b200 import synth
+    from oracle import sampler as OS
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = OS.Cfg(**WORKLOAD)
+    params, x0, prefix = synth.workload(cfg, seed=0, batch=1)
+    p = {k: v.bfloat16() for k, v in params.items()}
+    qp = OS.quantize_params(p, cfg, 4)
+    kv = OS.encode_prefix(p, cfg, prefix.bfloat16(), qp)
+    xb = x0.bfloat16()
+    for _ in range(max(args.warmup, 1)):
+        OS.flow_sample(p, cfg, xb, N_STEPS, kv, qp)
+    times = []
+    t_start = time.perf_counter()
+    for i in range(args.steps):
+        t0 = time.perf_counter()
+        OS.flow_sample(p, cfg, xb, N_STEPS, kv, qp)
+        times.append((time.perf_counter() - t0) * 1e3)
+        if time.perf_counter() - t_start > 150 and i >= 2:
+            break
+    v = statistics.mean(times)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "ms",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 3),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "action-expert sampler d1024 L4 h16x64 mlp4096 P256 H50 A32, "
+                               "batch 1, 10 Euler steps, int4 group-128", "weights": "int4",
+                   "batch": 1, "n_steps": N_STEPS},
+        "cpu_baseline": {"value": round(v, 3), "unit": "ms", "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"{len(times)} full sampler calls (oracle restatement of the "
+                                   "reference's dequantise-then-matmul eager loop, torch CPU)"},
+        "e2e": {"value": round(v, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    rank, world, local = dist_setup("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from embodied_efficiency_b200 import GraphedSampler, flow_sample
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    results = {}
+    experts = {}
+    for bits in (16, 8, 4):
+        m, x0, prefix = build_expert(bits, dev)
+        kv = m.encode(prefix.to(dev))
+        x = x0.to(dev).bfloat16()
+        plan = m.plan(1, kv)
+        out = torch.empty_like(x)
+        fn = lambda: plan.run(x, N_STEPS, out=out)  # noqa: E731
+        results[bits] = time_calls(fn, 20, args.warmup, flush)
+        experts[bits] = (m, x, kv, plan, out)
+
+    m, x, kv, plan, out = experts[4]
+    fn = lambda: plan.run(x, N_STEPS, out=out)  # noqa: E731
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        per_call = time_calls(fn, args.steps, args.warmup, flush)
+    total_ms = sum(per_call)
+    t_max = torch.tensor([total_ms], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t_max, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.barrier()
+    value = t_max.item() / (args.steps * world)
+    status = plan.status(N_STEPS)
+    if status != 0:
+        raise RuntimeError(f"sampler status {status}")
+
+    # e2e: GraphedSampler.run with a pinned host input, result copied back to the host
+    gs = GraphedSampler(m, x, N_STEPS)
+    xh = x.cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+
+    def e2e_call():
+        y = gs.run(xh)
+        yh.copy_(y, non_blocking=True)
+
+    e2e_ms = time_calls(e2e_call, args.steps, args.warmup, flush)
+    e2e_total = torch.tensor([sum(e2e_ms)], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(e2e_total, op=torch.distributed.ReduceOp.MAX)
+    e2e_value = e2e_total.item() / (args.steps * world)
+
+    if rank != 0:
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return
+
+    hbm, peak_kind = peaks()
+    wb, kvb = step_bytes(WORKLOAD, 4)
+    kernel_ms = statistics.mean(per_call)
+    achieved = wb * N_STEPS / (kernel_ms * 1e-3) / 1e9
+    variants = {}
+    for bits, ms in results.items():
+        w_b, _ = step_bytes(WORKLOAD, bits)
+        t = statistics.median(ms)
+        variants["bf16" if bits == 16 else f"int{bits}"] = {
+            "ms_per_call": round(t, 4), "weight_MB_per_step": round(w_b / 1e6, 2),
+            "weight_GBps": round(w_b * N_STEPS / (t * 1e-3) / 1e9, 1)}
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": "ms", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 4),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "action-expert sampler d1024 L4 h16x64 mlp4096 P256 H50 A32, "
+                               "batch 1, 10 Euler steps, int4 group-128",
+                   "weights": "int4", "batch": 1, "n_steps": N_STEPS,
+                   "parallelism": f"replicas x{world}",
+                   "l2": f"flushed between calls ({L2_FLUSH_BYTES >> 20} MiB write)"},
+        "e2e": {"value": round(e2e_value, 4), "unit": "ms", "h2d_bytes_per_step": xh.numel() * 2,
+                "d2h_bytes_per_step": yh.numel() * 2,
+                "path": "GraphedSampler.run(pinned host x) + copy of the result to pinned host"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "peak_kind": peak_kind,
+                     "kernel": "sampler_kernel (one launch per call)",
+                     "algorithmic_bytes_per_launch": wb * N_STEPS,
+                     "kv_bytes_per_launch": kvb * N_STEPS},
+        "variants": variants,
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    if not args.no_sweep:
+        line["gemm_k4096"] = gemm_sweep(dev, flush)
+    if not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        v, n = cpu_baseline_run()
+        line["cpu_baseline"] = {"value": round(v, 2), "unit": "ms", "cores": torch.get_num_threads(),
+                                "kind": "port",
+                                "sample": f"{n} full sampler calls of the same workload (oracle "
+                                          "restatement of the reference path, torch CPU, bf16)"}
+    print(json.dumps(line))
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,6 @@
+// ee_sampler_f16_64.cu -- sampler kernel instantiation: f16 activations, head size 64.
+#include "ee_sampler.cuh"
+
+namespace ee {
+template int launch_sampler<__half, 64>(const Ctx&, cudaStream_t);
+}  // namespace ee

@@ -1,0 +1,233 @@
+"""Flow-matching action expert and sampler: drop-in for the reference's
+``kernel/flow_expert.py`` surface.
+
+The module tree (names, registration order, shapes) is the reference's, so
+``state_dict``s interchange and ``torch.manual_seed(s); ActionExpert(cfg)``
+draws the same default-initialised weights. On CUDA, ``flow_sample`` /
+``ActionExpert.forward`` run the whole computation as one fused sm_100a launch
+(``ee_flow_sample``); configurations that launch does not cover run an eager
+GPU composition whose linears still go through ``ee_wq_gemm``. There is no
+CPU path.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _lib
+from . import fused as _fused
+from .wq_gemm import wq_linear
+
+
+@dataclass
+class ActionExpertConfig:
+    """kernel/flow_expert.py:28-35 plus two variant flags.
+
+    ``norm`` ("layernorm", the reference's, or "rmsnorm") and ``self_attn``
+    (False drops the action-token self-attention sub-block) describe the
+    pre-RMSNorm, cross-attention-only block variant; ``eps`` is the RMSNorm
+    epsilon (LayerNorm keeps nn.LayerNorm's 1e-5).
+    """
+
+    d_model: int = 512
+    n_layers: int = 6
+    n_heads: int = 8
+    horizon: int = 50
+    action_dim: int = 32
+    prefix_len: int = 256
+    mlp_ratio: float = 4.0
+    norm: str = "layernorm"
+    self_attn: bool = True
+    eps: float = 1e-5
+
+
+def timestep_embedding(t: torch.Tensor, dim: int, max_period: float = 10000.0) -> torch.Tensor:
+    """kernel/flow_expert.py:38-48: [cos, sin] of t * freqs * 1000, fp32. The fused
+    launch computes the same values in-kernel; this is the module-level helper."""
+    half = dim // 2
+    freqs = torch.exp(-math.log(max_period)
+                      * torch.arange(half, device=t.device, dtype=torch.float32) / half)
+    args = t.float()[:, None] * freqs[None] * 1000.0
+    emb = torch.cat([torch.cos(args), torch.sin(args)], dim=-1)
+    if dim % 2 == 1:
+        emb = torch.cat([emb, torch.zeros_like(emb[:, :1])], dim=-1)
+    return emb
+
+
+class RMSNorm(nn.Module):
+    """``(x * rsqrt(mean(x^2) + eps))`` rounded to x.dtype, times ``weight``."""
+
+    def __init__(self, d: int, eps: float = 1e-5):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(d))
+        self.eps = eps
+
+    def forward(self, x):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)).to(x.dtype) * self.weight
+
+
+def _norm(cfg):
+    return RMSNorm(cfg.d_model, cfg.eps) if getattr(cfg, "norm", "layernorm") == "rmsnorm" \
+        else nn.LayerNorm(cfg.d_model)
+
+
+def _apply_linear(mod, x):
+    """A linear of the eager path on the sm_100a GEMM (cuBLAS only for K % 128 != 0)."""
+    if isinstance(mod, nn.Linear):
+        if mod.in_features % 128 == 0 and x.dtype in (torch.bfloat16, torch.float16):
+            return wq_linear(x, mod.weight, None, mod.bias, 0, 16)
+        return F.linear(x, mod.weight, mod.bias)
+    return mod(x)
+
+
+class Block(nn.Module):
+    """kernel/flow_expert.py:51-95: pre-norm self-attention over the action chunk
+    (optional), cross-attention to the cached prefix, GELU MLP."""
+
+    def __init__(self, cfg: ActionExpertConfig):
+        super().__init__()
+        d, h = cfg.d_model, cfg.n_heads
+        assert d % h == 0
+        self.h, self.hd = h, d // h
+        if getattr(cfg, "self_attn", True):
+            self.n1 = _norm(cfg)
+            self.qkv = nn.Linear(d, 3 * d)
+            self.proj = nn.Linear(d, d)
+        else:
+            self.n1 = self.qkv = self.proj = None
+        self.nx = _norm(cfg)
+        self.q_c = nn.Linear(d, d)
+        self.kv_c = nn.Linear(d, 2 * d)
+        self.out_c = nn.Linear(d, d)
+        self.n2 = _norm(cfg)
+        hidden = int(d * cfg.mlp_ratio)
+        self.mlp = nn.Sequential(nn.Linear(d, hidden), nn.GELU(), nn.Linear(hidden, d))
+
+    def _split(self, x):
+        b, t, _ = x.shape
+        return x.view(b, t, self.h, self.hd).transpose(1, 2)
+
+    def _merge(self, x):
+        b, _, t, _ = x.shape
+        return x.transpose(1, 2).contiguous().view(b, t, self.h * self.hd)
+
+    def precompute_kv(self, prefix: torch.Tensor):
+        """kernel/flow_expert.py:78-81: prefix [B,P,D] -> (K, V) [B,h,P,hd], views of
+        one kv_c output."""
+        _lib.require_cuda(prefix)
+        k, v = _apply_linear(self.kv_c, prefix).chunk(2, dim=-1)
+        return self._split(k), self._split(v)
+
+    def forward(self, x: torch.Tensor, kv_c):
+        """Eager GPU composition (used only where the fused launch does not apply)."""
+        _lib.require_cuda(x)
+        if self.qkv is not None:
+            q, k, v = _apply_linear(self.qkv, self.n1(x)).chunk(3, dim=-1)
+            a = F.scaled_dot_product_attention(self._split(q), self._split(k), self._split(v))
+            x = x + _apply_linear(self.proj, self._merge(a))
+        q = self._split(_apply_linear(self.q_c, self.nx(x)))
+        a = F.scaled_dot_product_attention(q, kv_c[0], kv_c[1])
+        x = x + _apply_linear(self.out_c, self._merge(a))
+        x = x + _apply_linear(self.mlp[2], F.gelu(_apply_linear(self.mlp[0], self.n2(x))))
+        return x
+
+
+class ActionExpert(nn.Module):
+    """kernel/flow_expert.py:98-124."""
+
+    def __init__(self, cfg: ActionExpertConfig):
+        super().__init__()
+        self.cfg = cfg
+        d = cfg.d_model
+        self.in_proj = nn.Linear(cfg.action_dim, d)
+        self.t_proj = nn.Linear(d, d)
+        self.blocks = nn.ModuleList([Block(cfg) for _ in range(cfg.n_layers)])
+        self.out_norm = _norm(cfg)
+        self.out_proj = nn.Linear(d, cfg.action_dim)
+        # stand-in for the VLM prefix embedding (kernel/flow_expert.py:108-110)
+        self.register_buffer("_prefix", torch.randn(1, cfg.prefix_len, d) * 0.02, persistent=False)
+
+    def encode_prefix(self, batch: int):
+        """kernel/flow_expert.py:112-115: per-layer prefix K/V for a batch, computed once."""
+        prefix = self._prefix.to(self.out_norm.weight.dtype).expand(batch, -1, -1)
+        return [blk.precompute_kv(prefix) for blk in self.blocks]
+
+    def encode(self, prefix: torch.Tensor):
+        """Per-layer K/V of an explicit prefix [B, P, d] (one per request)."""
+        prefix = prefix.to(self.out_norm.weight.dtype)
+        return [blk.precompute_kv(prefix) for blk in self.blocks]
+
+    def plan(self, batch: int, prefix_kv):
+        """The fused-launch plan for this batch and prefix K/V (built once, cached)."""
+        return get_plan(self, batch, prefix_kv)
+
+    def forward(self, x_act: torch.Tensor, t: torch.Tensor, prefix_kv):
+        """kernel/flow_expert.py:117-124: velocity for x_act [B,H,A] at times t [B]."""
+        _lib.require_cuda(x_act)
+        b = x_act.shape[0]
+        if _fused.supports(self, b):
+            v = self.plan(b, prefix_kv).run(x_act, 1, t0=t, mode=_lib.EE_MODE_VELOCITY)
+            return v.to(x_act.dtype)
+        x = _apply_linear(self.in_proj, x_act)
+        temb = _apply_linear(self.t_proj, timestep_embedding(t, self.cfg.d_model).to(x.dtype))
+        x = x + temb[:, None, :]
+        for blk, kv in zip(self.blocks, prefix_kv):
+            x = blk(x, kv)
+        return _apply_linear(self.out_proj, self.out_norm(x))
+
+    @torch.no_grad()
+    def sample(self, prefix: torch.Tensor, steps: int = 10, x0: torch.Tensor | None = None):
+        """One sampler call from a raw prefix [B, P, d]: encode the prefix, then
+        ``steps`` Euler steps from x0 (N(0,1) noise when not given)."""
+        b = prefix.shape[0]
+        if x0 is None:
+            x0 = torch.randn(b, self.cfg.horizon, self.cfg.action_dim, device=prefix.device,
+                             dtype=self.out_norm.weight.dtype)
+        return flow_sample(self, x0, steps, self.encode(prefix))
+
+
+def get_plan(expert, batch: int, prefix_kv):
+    """Fused-launch plan of any action-expert module (this package's or the
+    reference's) for a batch and prefix K/V, cached on the module and rebuilt
+    when a parameter is replaced or modified in place."""
+    key = (batch, tuple(kv[0].data_ptr() for kv in prefix_kv),
+           tuple((p.data_ptr(), p._version) for p in expert.parameters()),
+           tuple(b.data_ptr() for b in expert.buffers()))
+    cache = expert.__dict__.setdefault("_ee_plans", {})
+    pl = cache.get(key)
+    if pl is None:
+        if len(cache) > 8:
+            cache.clear()
+        pl = _fused.FusedPlan(expert, batch, prefix_kv)
+        cache[key] = pl
+    return pl
+
+
+@torch.no_grad()
+def flow_sample(expert, x_init: torch.Tensor, n_steps: int, prefix_kv) -> torch.Tensor:
+    """kernel/flow_expert.py:127-137: Euler integration over n_steps, t in x.dtype.
+
+    On the fused path all n_steps run in one ``ee_flow_sample`` launch.
+    """
+    _lib.require_cuda(x_init)
+    b = x_init.shape[0]
+    if _fused.supports(expert, b):
+        return get_plan(expert, b, prefix_kv).run(x_init, n_steps).to(x_init.dtype)
+    x = x_init
+    dt = 1.0 / n_steps
+    t = torch.zeros(x.shape[0], device=x.device, dtype=x.dtype)
+    for _ in range(n_steps):
+        v = expert(x, t, prefix_kv)
+        x = x + v * dt
+        t = t + dt
+    return x
+
+
+def sample(expert, prefix: torch.Tensor, steps: int = 10, x0: torch.Tensor | None = None):
+    """Function form of ``ActionExpert.sample``."""
+    return expert.sample(prefix, steps, x0)

@@ -1,0 +1,68 @@
+"""Host-side weight quantisation (load time, not the timed path).
+
+Same names, signatures and arithmetic as the reference's ``kernel/quant.py``:
+fp32 amax, fp32 division, round-half-to-even, clamp, int8 storage, so the
+integers are bit-identical to the reference's on any device. The packed
+weights these produce are consumed by the sm_100a kernels in ``csrc/``.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+
+def quantize_weight(w: torch.Tensor, bits: int, group_size: int = 128):
+    """kernel/quant.py:22-30 -- symmetric per-group quantisation along the input dim.
+
+    w: [out, in] float. Returns (q int8 [out, in/gs, gs], scale fp32
+    [out, in/gs, 1], gs) with gs = group_size if in % group_size == 0 else in.
+    """
+    out, inf = w.shape
+    gs = group_size if inf % group_size == 0 else inf
+    wg = w.float().reshape(out, inf // gs, gs)
+    qmax = 2 ** (bits - 1) - 1
+    scale = (wg.abs().amax(dim=-1, keepdim=True) / qmax).clamp_min(1e-8)
+    q = torch.clamp(torch.round(wg / scale), -qmax - 1, qmax)
+    return q.to(torch.int8), scale, gs
+
+
+def dequantize_weight(q: torch.Tensor, scale: torch.Tensor, gs: int) -> torch.Tensor:
+    """kernel/quant.py:33-35."""
+    out, ng, _ = q.shape
+    return (q.float() * scale).view(out, ng * gs)
+
+
+def quantize_weight_asym4(w: torch.Tensor, group_size: int = 128):
+    """Asymmetric int4 with an fp16 scale and an fp16 (integer-valued) zero per group.
+
+    No reference counterpart (the reference quantises symmetrically only).
+    Per group: ``scale = fp16(max((max - min) / 15, 2^-14))``,
+    ``zero = clamp(round(-min / scale), 0, 15)``,
+    ``q = clamp(round(w / scale) + zero, 0, 15)``; dequantised ``(q - zero) * scale``.
+    Returns (q uint8 [out, in] in 0..15, scale fp16 [out, in/gs],
+    zero fp16 [out, in/gs], gs).
+    """
+    out, inf = w.shape
+    gs = group_size if inf % group_size == 0 else inf
+    wg = w.float().reshape(out, inf // gs, gs)
+    wmin = wg.amin(dim=-1, keepdim=True)
+    wmax = wg.amax(dim=-1, keepdim=True)
+    scale = ((wmax - wmin) / 15.0).clamp_min(2.0 ** -14).half().float()
+    zero = torch.clamp(torch.round(-wmin / scale), 0, 15)
+    q = torch.clamp(torch.round(wg / scale) + zero, 0, 15).to(torch.uint8)
+    return (q.reshape(out, inf), scale.reshape(out, -1).half(), zero.reshape(out, -1).half(), gs)
+
+
+def linear_bytes(model: nn.Module, dtype_bytes: int = 2) -> float:
+    """kernel/quant.py:76-77: dense linear weight bytes at ``dtype_bytes`` each."""
+    return sum(m.weight.numel() * dtype_bytes for m in model.modules() if isinstance(m, nn.Linear))
+
+
+def quant_linear_bytes(model: nn.Module) -> float:
+    """kernel/quant.py:58-59,80-81: int weights plus fp16-counted scales of every
+    quantised linear."""
+    tot = 0.0
+    for m in model.modules():
+        if hasattr(m, "weight_bytes") and callable(m.weight_bytes):
+            tot += m.weight_bytes()
+    return tot

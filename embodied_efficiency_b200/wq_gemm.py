@@ -1,0 +1,179 @@
+"""Weight-only int8 / int4 dequant-GEMM: drop-in for the reference's
+``kernel/triton_gemm.py`` surface, backed by the sm_100a kernels of
+``libee_b200.so`` (no Triton, no CPU path).
+
+Layouts are the reference's: int8 weights [N, K]; int4 packed two per byte
+[N, K/2] with the even k in the low nibble; fp32 scales [N, K/group].
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _lib
+from .quant import quantize_weight
+
+
+# ---------------------------------------------------------------------------
+# packing (bit-exact with kernel/triton_gemm.py:37-48), on the GPU
+# ---------------------------------------------------------------------------
+def _pack_int4(q2d: torch.Tensor) -> torch.Tensor:
+    """kernel/triton_gemm.py:37-39: int8 [N, K] in -8..7 -> uint8 [N, K/2]."""
+    _lib.require_cuda(q2d)
+    if q2d.dim() != 2 or q2d.shape[1] % 2:
+        raise ValueError("_pack_int4 expects [N, K] with K even")
+    q = q2d.to(torch.int8).contiguous()
+    out = torch.empty(q.shape[0], q.shape[1] // 2, dtype=torch.uint8, device=q.device)
+    _lib.check(_lib.load().ee_pack_int4(q.data_ptr(), out.data_ptr(), q.shape[0], q.shape[1],
+                                        _lib.stream_ptr(q.device)), "ee_pack_int4")
+    return out
+
+
+def _unpack_int4(packed: torch.Tensor) -> torch.Tensor:
+    """kernel/triton_gemm.py:42-48: uint8 [N, K/2] -> int8 [N, K] (sign-extended nibbles)."""
+    _lib.require_cuda(packed)
+    p = packed.to(torch.uint8).contiguous()
+    n, kh = p.shape
+    out = torch.empty(n, 2 * kh, dtype=torch.int8, device=p.device)
+    _lib.check(_lib.load().ee_unpack_int4(p.data_ptr(), out.data_ptr(), n, 2 * kh,
+                                          _lib.stream_ptr(p.device)), "ee_unpack_int4")
+    return out
+
+
+def _dequant_int8(q, scale, gs):
+    """kernel/triton_gemm.py:51-55 (reference helper, used only to check kernels)."""
+    n, k = q.shape
+    ng = scale.shape[1]
+    return (q.float().view(n, ng, gs) * scale.float().view(n, ng, 1)).view(n, k)
+
+
+def _dequant_int4(packed, scale, gs):
+    """kernel/triton_gemm.py:57-58."""
+    return _dequant_int8(_unpack_int4(packed), scale, gs)
+
+
+# ---------------------------------------------------------------------------
+# the fused dequant-GEMM
+# ---------------------------------------------------------------------------
+def wkind_for(bits: int, zeros=None) -> int:
+    if bits == 4:
+        return _lib.EE_W_UINT4Z if zeros is not None else _lib.EE_W_INT4
+    if bits == 8:
+        return _lib.EE_W_INT8
+    if bits == 16:
+        return _lib.EE_W_DENSE
+    raise ValueError(f"bits must be 4, 8 or 16, got {bits}")
+
+
+def wq_linear(x, weight, scales, bias, group_size, bits, zeros=None, gelu=False, residual=None):
+    """kernel/triton_gemm.py:141-164: ``x @ dequant(weight).T + bias`` in x.dtype.
+
+    Runs ``ee_wq_gemm``: dequantisation in registers, fp32 accumulation, bias
+    in fp32, one rounding to the activation dtype. bf16 / fp16 activations are
+    used as they are; fp32 activations are computed in bf16 and the result is
+    returned as fp32. Optional fused epilogues: ``gelu`` (exact erf GELU) or
+    ``residual`` (+ residual, both rounded as separate torch ops would).
+    ``bits=16`` means ``weight`` is a dense [N, K] matrix in the activation dtype.
+    """
+    _lib.require_cuda(x, weight)
+    *lead, k_in = x.shape
+    n = weight.shape[0]
+    k = weight.shape[1] * 2 if bits == 4 else weight.shape[1]
+    if k_in != k:
+        raise ValueError(f"x has K={k_in}, weight has K={k}")
+    out_dtype = x.dtype
+    act = x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
+    xf = x.reshape(-1, k).to(act).contiguous()
+    m = xf.shape[0]
+    if bits == 16:
+        weight = weight.to(act)
+    w = weight.contiguous()
+    s = None if scales is None else scales.contiguous()
+    z = None if zeros is None else zeros.to(torch.float16).contiguous()
+    b = None if bias is None else bias.to(act).contiguous()
+    r = None if residual is None else residual.reshape(m, n).to(act).contiguous()
+    y = torch.empty(m, n, dtype=act, device=x.device)
+    if m == 0:
+        return y.reshape(*lead, n).to(out_dtype)
+    epi = (_lib.EE_EPI_BIAS if b is not None else 0) | (_lib.EE_EPI_GELU if gelu else 0) | \
+        (_lib.EE_EPI_RESIDUAL if r is not None else 0)
+    rc = _lib.load().ee_wq_gemm(
+        xf.data_ptr(), w.data_ptr(), _lib.ptr(s), _lib.ptr(z), _lib.ptr(b), _lib.ptr(r), y.data_ptr(),
+        m, n, k, wkind_for(bits, z), int(group_size) if bits != 16 else 0, _lib.act_code(act),
+        _lib.scale_code(s.dtype) if s is not None else _lib.EE_F32, epi, _lib.stream_ptr(x.device))
+    _lib.check(rc, "ee_wq_gemm")
+    return y.reshape(*lead, n).to(out_dtype)
+
+
+class TritonQuantLinear(nn.Module):
+    """kernel/triton_gemm.py:167-184: weight-only int8 / int4 linear.
+
+    Same buffers and attributes as the reference (``weight``, ``scales``,
+    ``bias``, ``bits``, ``group_size``, ``in_features``, ``out_features``) so
+    that callers such as ``compiler._weight_mb`` see the same module; the
+    forward runs the sm_100a dequant-GEMM.
+    """
+
+    def __init__(self, lin: nn.Linear, bits: int = 8, group_size: int = 128):
+        super().__init__()
+        assert bits in (4, 8)
+        q3, scale3, gs = quantize_weight(lin.weight.data.float(), bits, group_size)
+        out, ng, g = q3.shape
+        q2d = q3.reshape(out, ng * g).to(torch.int8)
+        if bits == 4:
+            dev = q2d.device
+            if not q2d.is_cuda:
+                if not torch.cuda.is_available():
+                    raise RuntimeError("int4 packing runs on the GPU; no CUDA device is visible")
+                q2d = q2d.cuda()
+            weight = _pack_int4(q2d).to(dev)
+        else:
+            weight = q2d.contiguous()
+        self.register_buffer("weight", weight)
+        self.register_buffer("scales", scale3.reshape(out, ng).contiguous().float())
+        self.bias = lin.bias
+        self.bits, self.group_size = bits, gs
+        self.out_features, self.in_features = out, ng * g
+
+    def forward(self, x):
+        return wq_linear(x, self.weight, self.scales, self.bias, self.group_size, self.bits)
+
+    def weight_bytes(self) -> float:
+        """kernel/quant.py:58-59: int weights + scales counted as fp16."""
+        return self.out_features * self.in_features * self.bits / 8.0 + self.scales.numel() * 2
+
+    def extra_repr(self):
+        return f"in={self.in_features}, out={self.out_features}, bits={self.bits}, group={self.group_size}"
+
+
+def quantize_model_triton(model, bits=8, group_size=128, skip=("in_proj", "out_proj")):
+    """kernel/triton_gemm.py:187-195: swap every nn.Linear except ``skip`` for
+    ``TritonQuantLinear``, recursively; returns the mutated model."""
+    for name, mod in list(model.named_children()):
+        if name in skip:
+            continue
+        if isinstance(mod, nn.Linear):
+            setattr(model, name, TritonQuantLinear(mod, bits, group_size))
+        else:
+            quantize_model_triton(mod, bits, group_size, skip)
+    return model
+
+
+def correctness_check():
+    """kernel/triton_gemm.py:198-210 on the sm_100a kernels: fp16 X [50, 512],
+    nn.Linear(512, 1536), kernel vs torch dequant + F.linear, max abs < 0.5."""
+    torch.manual_seed(1)
+    x = torch.randn(50, 512, device="cuda", dtype=torch.float16)
+    errs = {}
+    for bits in (8, 4):
+        lin = nn.Linear(512, 1536).cuda().half()
+        ql = TritonQuantLinear(lin, bits).cuda()
+        y = wq_linear(x, ql.weight, ql.scales, ql.bias, ql.group_size, bits)
+        deq = (_dequant_int4 if bits == 4 else _dequant_int8)(ql.weight, ql.scales, ql.group_size)
+        err = (y - F.linear(x, deq.to(x.dtype), ql.bias)).abs().max().item()
+        print(f"  int{bits}: sm_100a kernel vs torch-dequant max abs err = {err:.4e}")
+        assert err < 5e-1, f"int{bits} kernel disagrees with reference"
+        errs[bits] = err
+    print("sm_100a dequant-GEMM correctness ok")
+    return errs

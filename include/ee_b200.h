@@ -1,0 +1,171 @@
+/*
+ * ee_b200.h -- C ABI of the B200 (sm_100a) weight-only dequant-GEMM and
+ * flow-matching sampler library (libee_b200.so).
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as an opaque pointer), returns EE_OK (0) or an error code and never
+ * aborts the process. Nothing here allocates device memory: scratch space is
+ * a caller-owned workspace, so the launch entry points can be captured into a
+ * CUDA graph. All device pointers must be 16-byte aligned.
+ *
+ * Reference interfaces replaced (LaelaZorana/embodied-efficiency):
+ *   ee_pack_int4          kernel/triton_gemm.py:37-39   _pack_int4
+ *   ee_unpack_int4        kernel/triton_gemm.py:42-48   _unpack_int4
+ *   ee_wq_gemm            kernel/triton_gemm.py:141-164 wq_linear
+ *                         (+ the Triton kernels at :75-138 it launches)
+ *   ee_flow_sample        kernel/flow_expert.py:127-137 flow_sample, run as
+ *                         one fused launch over kernel/flow_expert.py:117-124
+ *                         ActionExpert.forward and :83-95 Block.forward
+ *                         (mode EE_MODE_VELOCITY = one ActionExpert.forward)
+ *   ee_flow_sample_workspace_bytes   sizing helper for ee_flow_sample (new)
+ *   ee_check_expert       one-time validation of an expert description (new)
+ *   ee_read_status        device status word of a sampler workspace (new)
+ *   ee_barrier_selftest   bounded-wait self-test of the grid barrier (new)
+ *   ee_strerror / ee_version / ee_struct_size   (new)
+ */
+#ifndef EE_B200_H
+#define EE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* ee_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+  EE_OK = 0,
+  EE_ERR_ARG = 1,         /* null pointer / bad enum value                 */
+  EE_ERR_SHAPE = 2,       /* unsupported or inconsistent sizes             */
+  EE_ERR_ALIGN = 3,       /* pointer not 16-byte aligned                   */
+  EE_ERR_DTYPE = 4,       /* unsupported dtype combination                 */
+  EE_ERR_WORKSPACE = 5,   /* workspace missing or too small                */
+  EE_ERR_LAUNCH = 6,      /* CUDA launch / runtime error                   */
+  EE_ERR_TIMEOUT = 7,     /* a device-side wait gave up (status word)      */
+  EE_ERR_DEVICE = 8,      /* no device / not an sm_100 device              */
+  EE_ERR_UNSUPPORTED = 9  /* valid request this build does not implement   */
+};
+
+/* ---- dtype / weight-format enums --------------------------------------- */
+enum { EE_BF16 = 0, EE_F16 = 1, EE_F32 = 2 };
+
+/* weight formats (bits argument of ee_wq_gemm, wkind of ee_linear):
+ *  EE_W_DENSE  weight is [N,K] in the activation dtype (the "bf16" rows)
+ *  EE_W_INT8   int8 [N,K], symmetric, scale per (row, group)
+ *  EE_W_INT4   uint8 [N,K/2], two's-complement nibbles, even k in the low
+ *              nibble (kernel/triton_gemm.py:37-39), symmetric
+ *  EE_W_UINT4Z uint8 [N,K/2] unsigned nibbles with a zero point per group
+ *              (asymmetric int4; no counterpart in the reference)            */
+enum { EE_W_DENSE = 0, EE_W_INT8 = 1, EE_W_INT4 = 2, EE_W_UINT4Z = 3 };
+
+/* epilogue flags of ee_wq_gemm */
+enum { EE_EPI_BIAS = 1, EE_EPI_GELU = 2, EE_EPI_RESIDUAL = 4 };
+
+/* sampler modes */
+enum { EE_MODE_EULER = 0, EE_MODE_VELOCITY = 1 };
+
+/* norm kinds */
+enum { EE_NORM_LAYER = 0, EE_NORM_RMS = 1 };
+
+const char* ee_strerror(int code);
+int ee_version(void);
+/* sizeof of the ABI records, for binding checks: 0 ee_linear, 1 ee_norm,
+ * 2 ee_block, 3 ee_expert; 0 for any other value. */
+size_t ee_struct_size(int32_t which);
+
+/* ---- int4 packing (bit-exact with the reference) ----------------------- */
+/* q: int8 [n,k] (values in -8..7), packed: uint8 [n,k/2]; k even.           */
+int ee_pack_int4(const int8_t* q, uint8_t* packed, int64_t n, int64_t k, ee_stream_t stream);
+int ee_unpack_int4(const uint8_t* packed, int8_t* q, int64_t n, int64_t k, ee_stream_t stream);
+
+/* ---- fused weight-only dequant-GEMM ------------------------------------ */
+/*
+ * y[m,n] = epi( sum_k x[m,k] * dequant(W)[n,k] )   with x, y row-major.
+ *   x        [m,k] act dtype (EE_BF16 or EE_F16)
+ *   weight   see EE_W_* (reference layout, row n contiguous in k)
+ *   scales   [n, k/group] EE_F32 or EE_F16 (scale_dtype); NULL for dense
+ *   zeros    [n, k/group] fp16 integer-valued zero points (EE_W_UINT4Z only)
+ *   bias     [n] act dtype, used when epilogue has EE_EPI_BIAS
+ *   residual [m,n] act dtype, used when epilogue has EE_EPI_RESIDUAL
+ *   y        [m,n] act dtype (may alias residual)
+ * epi applies, in order: +bias, round to act dtype, then GELU(erf) or
+ * residual + value, each rounded to the act dtype (the reference's
+ * op-by-op rounding). Requires k % 128 == 0 and group % 128 == 0 (or
+ * group == k); m, n arbitrary >= 1.
+ */
+int ee_wq_gemm(const void* x, const void* weight, const void* scales, const void* zeros,
+               const void* bias, const void* residual, void* y,
+               int64_t m, int64_t n, int64_t k, int32_t wkind, int32_t group,
+               int32_t act_dtype, int32_t scale_dtype, int32_t epilogue, ee_stream_t stream);
+
+/* ---- fused flow-matching sampler --------------------------------------- */
+typedef struct ee_linear {
+  const void* weight; /* see EE_W_*                                       */
+  const void* scales; /* [n, k/group] (NULL for dense)                    */
+  const void* zeros;  /* [n, k/group] fp16 (EE_W_UINT4Z only, else NULL) */
+  const void* bias;   /* [n] act dtype or NULL                            */
+  int32_t n, k, wkind, group, scale_dtype, reserved;
+} ee_linear;
+
+typedef struct ee_norm {
+  const void* weight; /* [d] act dtype                  */
+  const void* bias;   /* [d] act dtype or NULL (RMSNorm) */
+} ee_norm;
+
+typedef struct ee_block {
+  ee_norm n1, nx, n2;
+  ee_linear qkv, proj, q_c, out_c, mlp0, mlp2;
+  const void* kv; /* prefix K/V cache: kv_c(prefix) output, [batch, prefix_len, 2*d] */
+} ee_block;
+
+typedef struct ee_expert {
+  int32_t d_model, n_layers, n_heads, horizon, action_dim, prefix_len, hidden, batch;
+  int32_t act_dtype, norm_kind, self_attn, reserved;
+  float eps, reserved_f;
+  const float* freqs; /* [d/2] fp32 time-embedding frequencies (kernel/flow_expert.py:41-43) */
+  ee_linear in_proj, t_proj, out_proj;
+  ee_norm out_norm;
+  const ee_block* blocks; /* DEVICE pointer to n_layers ee_block records */
+} ee_expert;
+
+/* Full validation of an expert description: every scalar field, and every
+ * block record from a HOST copy of the table that ex->blocks points to on
+ * the device. ee_flow_sample re-checks only the scalar fields (it never reads
+ * the device table on the host), so call this once when the table is built. */
+int ee_check_expert(const ee_expert* ex, const ee_block* host_blocks, int32_t n_steps, int32_t mode);
+
+/* Workspace bytes ee_flow_sample needs for this expert and step count. */
+size_t ee_flow_sample_workspace_bytes(const ee_expert* ex, int32_t n_steps);
+
+/*
+ * One sampler call as a single persistent launch (one CTA per SM, phases
+ * separated by bounded grid barriers).
+ *   x_in  [batch, horizon, action_dim] act dtype
+ *   t0    [batch] act dtype start times, or NULL for t = 0
+ *   x_out [batch, horizon, action_dim]: EE_MODE_EULER -> x after n_steps
+ *         Euler steps (dt = 1/n_steps, t and x kept in the act dtype);
+ *         EE_MODE_VELOCITY -> the velocity at (x_in, t0), n_steps must be 1.
+ * A device-side wait that exceeds its limit aborts the launch and leaves
+ * EE_ERR_TIMEOUT in the workspace status word (see ee_read_status).
+ */
+int ee_flow_sample(const ee_expert* ex, const void* x_in, const void* t0, void* x_out,
+                   int32_t n_steps, int32_t mode, void* workspace, size_t workspace_bytes,
+                   ee_stream_t stream);
+
+/* Self-test of the bounded device-side wait: launches one CTA that waits at a
+ * grid barrier no other CTA reaches, so the wait ends only by its limit
+ * (timeout_ns, at most 2 s) and leaves EE_ERR_TIMEOUT in the status word of
+ * `workspace` (>= 256 bytes, read it with ee_read_status). */
+int ee_barrier_selftest(void* workspace, uint64_t timeout_ns, ee_stream_t stream);
+
+/* Synchronises `stream` and copies the workspace status word to *status. */
+int ee_read_status(const void* workspace, int32_t* status, ee_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EE_B200_H */
