@@ -95,6 +95,11 @@ EE_DEV uint32_t ld_act4(const void* p) {
   return r;
 }
 
+EE_DEV float ld_act_f32(const float* p) {
+  float r;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(r) : "l"(p) : "memory");
+  return r;
+}
 template <typename T> EE_DEV float ld_act_scalar(const T* p) {
   uint16_t b = ld_act2(p);
   return Act<T>::to_f(*reinterpret_cast<T*>(&b));
@@ -244,11 +249,19 @@ EE_DEV float4 ld_dsmem_f4(uint32_t addr) {
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
   return v;
 }
+EE_DEV float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
 EE_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 EE_DEV void cp_async16(uint32_t dst, const void* src, bool valid) {
   const int n = valid ? 16 : 0;
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n)
                : "memory");
+}
+EE_DEV void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
 }
 EE_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N> EE_DEV void cp_async_wait() {

@@ -44,26 +44,68 @@ struct GemmArgs {
   const void* resid;   // [M, N] residual input (EPI_RESID), row stride ldr
   long long ldr;
   int has_bias;
-  // optional normalisation of finished rows (sampler residual phases)
-  const void* ln_w;
-  const void* ln_b;
-  void* ln_out;        // [M, N] normalised rows; NULL = none
-  unsigned* ln_cnt;    // one arrival counter per 64-token tile
-  int norm_kind;
-  float eps;
+  int split;           // CTAs of a cluster per unit (a power of two dividing the cluster)
+  int lsplit;          // log2(split)
+  // Row statistics are kept as partial (sum, sum of squares) per 128-column
+  // tile of the row: [M][stat_slots][2], summed in slot order (deterministic).
+  int stat_slots;
+  // input normalisation: when in_stats is set, every staged activation row is
+  // normalised with its statistics over K and the weight / bias in_w / in_b
+  // (LayerNorm) or in_w only (RMSNorm) before the MMAs
+  const float* in_stats;  // [M][stat_slots][2]
+  const void* in_w;
+  const void* in_b;
+  int in_norm;            // EE_NORM_*
+  float in_eps;
+  // output statistics: when out_stats is set, each unit writes the (sum, sum
+  // of squares) of its 128 output columns of every token row to slot n-tile
+  float* out_stats;       // [M][stat_slots][2]
 };
 
-// Shared memory of a GEMM unit. X holds the activation slice [64 tok][KS]
-// (16-byte chunks swizzled, see x_chunk); after the MMAs the same bytes hold
-// the reduced tile E[64][128/CL] and the row buffers of the norm. P is this
-// CTA's partial tile [128 rows][kPS]. PRE holds weight words prefetched
-// before a grid barrier.
+// Shared memory of a GEMM unit (byte offsets from the dynamic base).
+//   x    activation slice [64 tok][KS] (16-byte chunks swizzled, see
+//        x_chunk); after the MMAs it holds the reduced tile E[64][128/S]
+//   p    this CTA's partial tile [128 rows][kPS] fp32
+//   aux  norm weight/bias slice, row statistics, bias, output-stat partials
+//        and the residual tile of the unit
+//   pre  weight words of the first unit, copied in before a grid barrier
 struct GemmSmem {
-  uint32_t x, p, pre;  // byte offsets
+  uint32_t x, p, aux, pre;
+  uint32_t pre_bytes;  // size of the pre area (0: no prefetch)
 };
+constexpr uint32_t kAuxGB = 0;                 // [2][2048] act: norm weight, bias slice
+constexpr uint32_t kAuxRow = 8192;             // [64][2] float: mean, rstd
+constexpr uint32_t kAuxBias = kAuxRow + 512;   // [128] float
+constexpr uint32_t kAuxOst = kAuxBias + 512;   // [64][2] float: output-stat partials
+constexpr uint32_t kAuxRes = kAuxOst + 512;    // [64][128] act: residual tile
+constexpr uint32_t kAuxScale = kAuxRes + 64 * 128 * 2;  // [kMaxKB][2][8 warps][8 g] float
+constexpr int kMaxKB = 16;                     // k-blocks per CTA with staged scales
+constexpr uint32_t kAuxBytes = kAuxScale + kMaxKB * 2 * 64 * 4;
+constexpr int kMaxNormSlice = 2048;            // K/S limit of a normalised input
 __host__ __device__ constexpr size_t gemm_x_bytes(int ks) { return (size_t)kMTile * ks * 2; }
 constexpr size_t kPBytes = (size_t)kRU * kPS * 4;
-constexpr size_t kPreBytes = (size_t)kThreads * 2 * 4 * 16;  // 2 rows x 4 words x 16 B
+__host__ __device__ constexpr size_t pre_kb_bytes(int kind) {  // prefetch bytes per k-block
+  return (size_t)kThreads * 2 * (kind == EE_W_DENSE ? 4 : (kind == EE_W_INT8 ? 2 : 1)) * 16;
+}
+
+// split policy: CTAs per unit S (a power of two dividing the cluster, K/S a
+// multiple of 128 and at most ks_cap) with the fewest rounds over the
+// cluster slots; ties go to the larger S (less work per CTA)
+__host__ __device__ inline int pick_split(int n, int k, int m, int nclusters, int cl, int ks_cap) {
+  const long long units = (long long)((n + kRU - 1) / kRU) * ((m + kMTile - 1) / kMTile);
+  int best = 0;
+  long long best_rounds = 0;
+  for (int sp = cl; sp >= 1; sp >>= 1) {
+    if ((k % (sp * kKBlock)) != 0 || k / sp > ks_cap) continue;
+    const long long slots = (long long)nclusters * (cl / sp);
+    const long long rounds = (units + slots - 1) / slots;
+    if (best == 0 || rounds < best_rounds) {
+      best = sp;
+      best_rounds = rounds;
+    }
+  }
+  return best;
+}
 
 __host__ __device__ constexpr int words_per_row(int kind) {
   return kind == EE_W_DENSE ? 4 : (kind == EE_W_INT8 ? 2 : 1);
@@ -80,68 +122,7 @@ EE_DEV uint32_t comp(const uint4& v, int c) {
 // row `row`: spreads the 8 threads of a quarter-warp over all bank groups
 EE_DEV int x_chunk(int row, int c) { return c ^ (((c >> 3) & 1) << 1) ^ (row & 1); }
 
-// Normalise `rows` token rows of x (row stride ldx, width d) into out:
-// LayerNorm (two-pass fp32 statistics, as torch's CPU kernel) or RMSNorm
-// (x * rsqrt(mean(x^2) + eps) rounded, times weight). One warp per row, the
-// row staged in `buf` (d floats per warp, shared memory).
-template <typename T>
-EE_DEV void norm_rows(const T* x, long long ldx, int row0, int rows, int d, const T* w,
-                      const T* b, int kind, float eps, T* out, long long ldo, float* buf) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* rb = buf + (size_t)warp * d;
-  const float inv_d = 1.0f / (float)d;
-  for (int r = warp; r < rows; r += kWarps) {
-    const T* xr = x + (size_t)(row0 + r) * ldx;
-    float s = 0.f;
-    for (int c = lane; c < d / 8; c += 32) {
-      const uint4 q = ld_act16(xr + c * 8);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = Act<T>::unpack2(comp(q, e));
-        rb[c * 8 + 2 * e] = f.x;
-        rb[c * 8 + 2 * e + 1] = f.y;
-        s += kind == EE_NORM_RMS ? f.x * f.x + f.y * f.y : f.x + f.y;
-      }
-    }
-    __syncwarp();
-    s = warp_sum(s);
-    float mean = 0.f, rstd;
-    if (kind == EE_NORM_RMS) {
-      rstd = 1.0f / sqrtf(s * inv_d + eps);
-    } else {
-      mean = s * inv_d;
-      float q = 0.f;
-      for (int i = lane; i < d; i += 32) q += (rb[i] - mean) * (rb[i] - mean);
-      rstd = 1.0f / sqrtf(warp_sum(q) * inv_d + eps);
-    }
-    __syncwarp();
-    T* orow = out + (size_t)(row0 + r) * ldo;
-    for (int c = lane; c < d / 8; c += 32) {
-      const uint4 wq = __ldg(reinterpret_cast<const uint4*>(w + c * 8));
-      const uint4 bq = b ? __ldg(reinterpret_cast<const uint4*>(b + c * 8)) : make_uint4(0, 0, 0, 0);
-      uint32_t o[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 wf = Act<T>::unpack2(comp(wq, e));
-        const float2 bf = Act<T>::unpack2(comp(bq, e));
-        const float v0 = rb[c * 8 + 2 * e], v1 = rb[c * 8 + 2 * e + 1];
-        float y0, y1;
-        if (kind == EE_NORM_RMS) {
-          y0 = Act<T>::round(v0 * rstd) * wf.x;
-          y1 = Act<T>::round(v1 * rstd) * wf.y;
-        } else {
-          y0 = (v0 - mean) * rstd * wf.x + bf.x;
-          y1 = (v1 - mean) * rstd * wf.y + bf.y;
-        }
-        o[e] = Act<T>::pack2(y0, y1);
-      }
-      *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-    __syncwarp();
-  }
-}
-
-// scales / zero points of a prefetched first k-block, kept in registers
+// scales / zero points of the prefetched first k-block, kept in registers
 struct PreRegs {
   float s[2];
   float z[2];
@@ -151,7 +132,7 @@ template <typename T, int KIND>
 struct Gemm {
   static constexpr int WPR = words_per_row(KIND);
 
-  // k-block kb (absolute, in 128s) of rows n (warp's g) and n+8, clamped to N
+  // k-block kb (absolute, in 128s) of row n, this thread's 32 k; n clamped to N
   static EE_DEV const char* row_ptr(const ee_linear& L, int n, int kb) {
     const int t = threadIdx.x & 3;
     n = n < L.n ? n : L.n - 1;
@@ -179,18 +160,8 @@ struct Gemm {
       load_scales(L, nw + g + 8 * h, kb, s[h], z[h]);
     }
   }
-  // cp.async the words of k-block kb into the prefetch area; scales to regs
-  static EE_DEV void prefetch(const ee_linear& L, int nw, int kb, uint32_t spre, PreRegs& pr) {
-    const int g = (threadIdx.x & 31) >> 2;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const char* p = row_ptr(L, nw + g + 8 * h, kb);
-#pragma unroll
-      for (int i = 0; i < WPR; ++i)
-        cp_async16(spre + ((h * 4 + i) * kThreads + threadIdx.x) * 16, p + 16 * i, true);
-      load_scales(L, nw + g + 8 * h, kb, pr.s[h], pr.z[h]);
-    }
-    cp_async_commit();
+  static EE_DEV uint32_t pre_addr(uint32_t spre, int kb, int h, int i) {
+    return spre + (uint32_t)((((kb * 2 + h) * WPR + i) * kThreads + threadIdx.x) * 16);
   }
 
   // raw words -> A-operand registers A[s][0..3] for the 8 mma steps
@@ -235,174 +206,366 @@ struct Gemm {
     }
   }
 
-  // Rows nt*128 .. +127 x tokens m0 .. m0+63 over all of K by this cluster.
-  // pre != nullptr: this CTA's first k-block was prefetched into sm.pre.
-  static EE_DEV void unit(const GemmArgs& a, int nt, int m0, char* smem, const GemmSmem& sm,
-                          const PreRegs* pre) {
+  // Start copying this CTA's first k-blocks of n-tile `nt` into the pre area
+  // (one cp.async group); scales of the first k-block go to pr.
+  static EE_DEV void prefetch(const GemmArgs& a, int nt, const GemmSmem& sm, uint32_t sbase,
+                              PreRegs& pr) {
+    const int rank = (int)cl_rank();
+    const int KB = (a.w.k >> a.lsplit) / kKBlock, kb0 = (rank & (a.split - 1)) * KB;
+    const int fit = (int)(sm.pre_bytes / pre_kb_bytes(KIND));
+    const int npre = KB < fit ? KB : fit;
+    const int nw = nt * kRU + 16 * (threadIdx.x >> 5), g = (threadIdx.x & 31) >> 2;
+    for (int kb = 0; kb < npre; ++kb)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const char* p = row_ptr(a.w, nw + g + 8 * h, kb0 + kb);
+#pragma unroll
+        for (int i = 0; i < WPR; ++i) cp_async16(pre_addr(sbase + sm.pre, kb, h, i), p + 16 * i, true);
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) load_scales(a.w, nw + g + 8 * h, kb0, pr.s[h], pr.z[h]);
+    cp_async_commit();
+  }
+
+  // One unit: rows nt*128 .. +127 x tokens m0 .. m0+63 over all of K, by the S
+  // CTAs of sub-cluster rank/S. Every CTA of the cluster calls this the same
+  // number of times (inactive CTAs only join the cluster barriers).
+  static EE_DEV void unit(const GemmArgs& a, bool active, int nt, int m0, char* smem,
+                          const GemmSmem& sm, const PreRegs* pre) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const ee_linear& L = a.w;
-    const int CL = (int)cl_size(), rank = (int)cl_rank();
-    const int KS = L.k / CL, KB = KS / kKBlock, kb0 = rank * KB;
-    const int mrows = min(kMTile, a.M - m0);
+    const int S = a.split, rank = (int)cl_rank();
+    const int sub0 = rank & ~(S - 1), r = rank - sub0;
+    const int KS = L.k >> a.lsplit, KB = KS / kKBlock, kb0 = r * KB;
+    const int RPR = kRU >> a.lsplit;  // rows this CTA reduces and stores
+    const int mrows = active ? min(kMTile, a.M - m0) : 0;
     const int JT = (mrows + 7) >> 3;
     const int nw = nt * kRU + 16 * warp;
+    const int nbase = nt * kRU + r * RPR;
     const uint32_t sbase = smem_u32(smem);
     const uint32_t sx = sbase + sm.x;
+    char* aux = smem + sm.aux;
+    float* rowst = reinterpret_cast<float*>(aux + kAuxRow);
+    float* sbias = reinterpret_cast<float*>(aux + kAuxBias);
+    float* ost = reinterpret_cast<float*>(aux + kAuxOst);
+    T* sres = reinterpret_cast<T*>(aux + kAuxRes);
 
-    // 1. this CTA's activation slice -> shared memory (rows >= mrows zeroed)
-    {
+    float acc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[j][c] = 0.f;
+
+    // weights: prefetched before the grid barrier, or requested now
+    PreRegs pr_local;
+    const PreRegs* prw = pre;
+    if (active && !pre && sm.pre_bytes >= pre_kb_bytes(KIND)) {
+      prefetch(a, nt, sm, sbase, pr_local);
+      prw = &pr_local;
+    }
+    const int fit = (int)(sm.pre_bytes / pre_kb_bytes(KIND));
+    const int npre = prw ? (KB < fit ? KB : fit) : 0;
+    // fp32 scales of every k-block are staged in shared memory
+    const bool smem_scales = KIND != EE_W_DENSE && L.scale_dtype == EE_F32 && KB <= kMaxKB;
+    float* ssc = reinterpret_cast<float*>(aux + kAuxScale);  // [kb][h][warp][g]
+
+    if (active) {
+      // 1. activation slice, norm weight / bias slice, residual tile -> smem
       const int cpr = KS / 8;  // 16-byte chunks per token row
       const char* xb = reinterpret_cast<const char*>(a.x);
       for (int i = threadIdx.x; i < JT * 8 * cpr; i += kThreads) {
         const int row = i / cpr, c = i - row * cpr;
         const bool ok = row < mrows;
         const char* src = xb + ((size_t)(m0 + (ok ? row : 0)) * a.ldx + (size_t)kb0 * kKBlock + c * 8) * 2;
-        const uint32_t dst = sx + (uint32_t)(row * KS * 2 + ((c >> 4) * 16 + x_chunk(row, c & 15)) * 16);
-        cp_async16(dst, src, ok);
+        cp_async16(sx + (uint32_t)(row * KS * 2 + ((c >> 4) * 16 + x_chunk(row, c & 15)) * 16), src, ok);
+      }
+      if (a.in_stats) {
+        const uint32_t sg = sbase + sm.aux + kAuxGB;
+        for (int i = threadIdx.x; i < 2 * cpr; i += kThreads) {
+          const int which = i / cpr, c = i - which * cpr;
+          const void* vec = which == 0 ? a.in_w : a.in_b;
+          const bool ok = vec != nullptr;
+          const char* src = reinterpret_cast<const char*>(ok ? vec : a.in_w) + ((size_t)kb0 * kKBlock + c * 8) * 2;
+          cp_async16(sg + (uint32_t)((which * kMaxNormSlice + c * 8) * 2), src, ok);
+        }
+      }
+      if (a.epi == EPI_RESID) {
+        const int rcpr = RPR / 8;  // 16-byte chunks of a residual row segment
+        const char* rb = reinterpret_cast<const char*>(a.resid);
+        for (int i = threadIdx.x; i < mrows * rcpr; i += kThreads) {
+          const int row = i / rcpr, c = i - row * rcpr;
+          const bool ok = nbase + c * 8 + 8 <= L.n;
+          const char* src = rb + ((size_t)(m0 + row) * a.ldr + (ok ? nbase + c * 8 : 0)) * 2;
+          cp_async16(sbase + sm.aux + kAuxRes + (uint32_t)((row * RPR + c * 8) * 2), src, ok);
+        }
+      }
+      if (smem_scales && t == 0) {
+        const int ng = L.k / L.group;
+        const float* sp = reinterpret_cast<const float*>(L.scales);
+        for (int kb = 0; kb < KB; ++kb)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            int n = nw + g + 8 * h;
+            n = n < L.n ? n : L.n - 1;
+            cp_async4(sbase + sm.aux + kAuxScale + (uint32_t)((((kb * 2 + h) * kWarps + warp) * 8 + g) * 4),
+                      sp + (size_t)n * ng + ((kb0 + kb) * kKBlock) / L.group);
+          }
       }
       cp_async_commit();
+      if (threadIdx.x < RPR) {
+        const int n = nbase + threadIdx.x;
+        sbias[threadIdx.x] = (a.has_bias && n < L.n) ? ld_param(reinterpret_cast<const T*>(L.bias) + n) : 0.f;
+      }
+      if (a.in_stats && threadIdx.x < mrows) {
+        const float* sp = a.in_stats + 2 * (size_t)(m0 + threadIdx.x) * a.stat_slots;
+        float2 st = make_float2(0.f, 0.f);
+        for (int q = 0; q < a.stat_slots; ++q) {  // fixed order: deterministic
+          st.x += ld_act_f32(sp + 2 * q);
+          st.y += ld_act_f32(sp + 2 * q + 1);
+        }
+        const float inv_k = 1.0f / (float)L.k;
+        float mean = 0.f, rstd;
+        if (a.in_norm == EE_NORM_RMS) {
+          rstd = 1.0f / sqrtf(st.y * inv_k + a.in_eps);
+        } else {
+          mean = st.x * inv_k;
+          const float var = fmaxf(st.y * inv_k - mean * mean, 0.f);
+          rstd = 1.0f / sqrtf(var + a.in_eps);
+        }
+        rowst[2 * threadIdx.x] = mean;
+        rowst[2 * threadIdx.x + 1] = rstd;
+      }
     }
-    // 2. first k-block of weights
+    // 2. weights of the first k-block (from the pre area, or loaded now)
     uint4 w[2][WPR];
     float sc[2] = {1.f, 1.f}, zr[2] = {0.f, 0.f};
-    if (pre) {
-      cp_async_wait<1>();  // the prefetch group (issued before the X group)
+    if (active) {
+      cp_async_wait<0>();
+      if (prw) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < 2; ++h) {
 #pragma unroll
-        for (int i = 0; i < WPR; ++i)
-          w[h][i] = lds16(sbase + sm.pre + ((h * 4 + i) * kThreads + threadIdx.x) * 16);
-        sc[h] = pre->s[h];
-        zr[h] = pre->z[h];
+          for (int i = 0; i < WPR; ++i) w[h][i] = lds16(pre_addr(sbase + sm.pre, 0, h, i));
+          sc[h] = prw->s[h];
+          zr[h] = prw->z[h];
+        }
+      } else {
+        load_raw(L, nw, kb0, w, sc, zr);
       }
-    } else {
-      load_raw(L, nw, kb0, w, sc, zr);
     }
-    cp_async_wait<0>();
     __syncthreads();
 
-    // 3. MMAs over this CTA's k-blocks
-    float acc[8][4];
+    if (active) {
+      // 3. normalise the staged activations in place
+      if (a.in_stats) {
+        const int cpr = KS / 8;
+        const T* sgw = reinterpret_cast<const T*>(aux + kAuxGB);
+        const T* sgb = sgw + kMaxNormSlice;
+        for (int i = threadIdx.x; i < mrows * cpr; i += kThreads) {
+          const int row = i / cpr, pc = i - row * cpr;
+          const int c = (pc & ~15) + x_chunk(row, pc & 15);  // logical chunk of physical pc
+          uint4* q = reinterpret_cast<uint4*>(smem + sm.x + row * KS * 2 + pc * 16);
+          const uint4 v = *q;
+          const uint4 wv = *reinterpret_cast<const uint4*>(sgw + c * 8);
+          const uint4 bv = *reinterpret_cast<const uint4*>(sgb + c * 8);
+          const float mean = rowst[2 * row], rstd = rowst[2 * row + 1];
+          uint32_t o[4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+          for (int e = 0; e < 4; ++e) {
+            const float2 xv = Act<T>::unpack2(comp(v, e));
+            const float2 wf = Act<T>::unpack2(comp(wv, e));
+            if (a.in_norm == EE_NORM_RMS) {
+              o[e] = Act<T>::pack2(Act<T>::round(xv.x * rstd) * wf.x, Act<T>::round(xv.y * rstd) * wf.y);
+            } else {
+              const float2 bf = Act<T>::unpack2(comp(bv, e));
+              o[e] = Act<T>::pack2((xv.x - mean) * rstd * wf.x + bf.x, (xv.y - mean) * rstd * wf.y + bf.y);
+            }
+          }
+          *q = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        __syncthreads();
+      }
+
+      // 4. MMAs over this CTA's k-blocks (first pre_kb from the pre area)
+      for (int kb = 0; kb < KB; ++kb) {
+        uint32_t A[8][4];
+        dequant(w, zr, A);
+        const float s0 = sc[0], s1 = sc[1];
+        if (kb + 1 < KB) {
+          if (kb + 1 < npre) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) acc[j][c] = 0.f;
-    for (int kb = 0; kb < KB; ++kb) {
-      uint32_t A[8][4];
-      dequant(w, zr, A);
-      const float s0 = sc[0], s1 = sc[1];
-      if (kb + 1 < KB) load_raw(L, nw, kb0 + kb + 1, w, sc, zr);
+            for (int h = 0; h < 2; ++h) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (j < JT) {
-          const int row = 8 * j + g;
-          const uint32_t rbase = sx + (uint32_t)(row * KS * 2 + kb * 256);
-          uint4 xq[4];
-#pragma unroll
-          for (int s2 = 0; s2 < 4; ++s2) xq[s2] = lds16(rbase + x_chunk(row, 4 * t + s2) * 16);
-          if (KIND == EE_W_DENSE) {
-#pragma unroll
-            for (int s = 0; s < 8; ++s)
-              mma16816<T>(acc[j], A[s][0], A[s][1], A[s][2], A[s][3], comp(xq[s >> 1], 2 * (s & 1)),
-                          comp(xq[s >> 1], 2 * (s & 1) + 1));
+              for (int i = 0; i < WPR; ++i) w[h][i] = lds16(pre_addr(sbase + sm.pre, kb + 1, h, i));
+              if (smem_scales) {
+                sc[h] = ssc[(((kb + 1) * 2 + h) * kWarps + warp) * 8 + g];
+                if (KIND == EE_W_UINT4Z)
+                  zr[h] = __half2float(__ldg(reinterpret_cast<const __half*>(L.zeros) +
+                                             (size_t)min(nw + g + 8 * h, L.n - 1) * (L.k / L.group) +
+                                             ((kb0 + kb + 1) * kKBlock) / L.group));
+              } else {
+                load_scales(L, nw + g + 8 * h, kb0 + kb + 1, sc[h], zr[h]);
+              }
+            }
           } else {
-            float p[4] = {0.f, 0.f, 0.f, 0.f};
+            load_raw(L, nw, kb0 + kb + 1, w, sc, zr);
+          }
+        }
 #pragma unroll
-            for (int s = 0; s < 8; ++s)
-              mma16816<T>(p, A[s][0], A[s][1], A[s][2], A[s][3], comp(xq[s >> 1], 2 * (s & 1)),
-                          comp(xq[s >> 1], 2 * (s & 1) + 1));
-            acc[j][0] += s0 * p[0];
-            acc[j][1] += s0 * p[1];
-            acc[j][2] += s1 * p[2];
-            acc[j][3] += s1 * p[3];
+        for (int j = 0; j < 8; ++j) {
+          if (j < JT) {
+            const int row = 8 * j + g;
+            const uint32_t rbase = sx + (uint32_t)(row * KS * 2 + kb * 256);
+            uint4 xq[4];
+#pragma unroll
+            for (int s2 = 0; s2 < 4; ++s2) xq[s2] = lds16(rbase + x_chunk(row, 4 * t + s2) * 16);
+            if (KIND == EE_W_DENSE) {
+#pragma unroll
+              for (int s = 0; s < 8; ++s)
+                mma16816<T>(acc[j], A[s][0], A[s][1], A[s][2], A[s][3], comp(xq[s >> 1], 2 * (s & 1)),
+                            comp(xq[s >> 1], 2 * (s & 1) + 1));
+            } else {
+              // two independent chains (steps 0-3, 4-7) halve the MMA dependency depth
+              float p[4] = {0.f, 0.f, 0.f, 0.f}, q[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+              for (int s = 0; s < 4; ++s) {
+                mma16816<T>(p, A[s][0], A[s][1], A[s][2], A[s][3], comp(xq[s >> 1], 2 * (s & 1)),
+                            comp(xq[s >> 1], 2 * (s & 1) + 1));
+                mma16816<T>(q, A[s + 4][0], A[s + 4][1], A[s + 4][2], A[s + 4][3],
+                            comp(xq[(s + 4) >> 1], 2 * (s & 1)), comp(xq[(s + 4) >> 1], 2 * (s & 1) + 1));
+              }
+              acc[j][0] += s0 * (p[0] + q[0]);
+              acc[j][1] += s0 * (p[1] + q[1]);
+              acc[j][2] += s1 * (p[2] + q[2]);
+              acc[j][3] += s1 * (p[3] + q[3]);
+            }
           }
         }
       }
-    }
 
-    // 4. partial tile -> P, then cluster-wide reduction over DSMEM
-    float* P = reinterpret_cast<float*>(smem + sm.p);
+      // 5. partial tile -> P
+      float* P = reinterpret_cast<float*>(smem + sm.p);
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (j < JT) {
-        const int r0 = 16 * warp + g, c0 = 8 * j + 2 * t;
-        *reinterpret_cast<float2*>(P + r0 * kPS + c0) = make_float2(acc[j][0], acc[j][1]);
-        *reinterpret_cast<float2*>(P + (r0 + 8) * kPS + c0) = make_float2(acc[j][2], acc[j][3]);
-      }
+      for (int j = 0; j < 8; ++j)
+        if (j < JT) {
+          const int r0 = 16 * warp + g, c0 = 8 * j + 2 * t;
+          *reinterpret_cast<float2*>(P + r0 * kPS + c0) = make_float2(acc[j][0], acc[j][1]);
+          *reinterpret_cast<float2*>(P + (r0 + 8) * kPS + c0) = make_float2(acc[j][2], acc[j][3]);
+        }
+    }
     cluster_sync();
-    const int RPR = kRU / CL;  // rows reduced by this rank
+
+    // 6. reduce this CTA's RPR rows over the S partial tiles of the sub-cluster
     float* E = reinterpret_cast<float*>(smem + sm.x);  // [64][RPR], reuses the X slice
-    const uint32_t pbase = sbase + sm.p;
-    for (int i = threadIdx.x; i < RPR * 16; i += kThreads) {
-      const int row = i >> 4, c4 = i & 15;
-      if (4 * c4 < JT * 8) {
-        const uint32_t off = (uint32_t)(((rank * RPR + row) * kPS + 4 * c4) * 4);
-        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int r = 0; r < CL; ++r) {
-          const float4 v = ld_dsmem_f4(mapa(pbase + off, (uint32_t)r));
-          sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
-        }
-        E[(4 * c4 + 0) * RPR + row] = sum.x;
-        E[(4 * c4 + 1) * RPR + row] = sum.y;
-        E[(4 * c4 + 2) * RPR + row] = sum.z;
-        E[(4 * c4 + 3) * RPR + row] = sum.w;
-      }
-    }
-    cluster_sync();  // peers done with this CTA's P; E complete in this CTA
-
-    // 5. epilogue: bias, round, GELU / residual, store
-    T* out = reinterpret_cast<T*>(a.out);
-    const T* bias = a.has_bias ? reinterpret_cast<const T*>(L.bias) : nullptr;
-    const int nbase = nt * kRU + rank * RPR;
-    for (int i = threadIdx.x; i < mrows * RPR; i += kThreads) {
-      const int tok = i / RPR, row = i - tok * RPR;
-      const int n = nbase + row;
-      if (n < L.n) {
-        float v = E[tok * RPR + row];
-        if (bias) v += ld_param(bias + n);
-        v = Act<T>::round(v);
-        const size_t m = (size_t)(m0 + tok);
-        if (a.epi == EPI_GELU) {
-          v = gelu_erf(v);
-        } else if (a.epi == EPI_RESID) {
-          v = ld_act_scalar(reinterpret_cast<const T*>(a.resid) + m * a.ldr + n) + v;
-        }
-        out[m * a.ldo + n] = Act<T>::from_f(v);
-      }
-    }
-
-    // 6. the last CTA to finish a token tile normalises its rows
-    if (a.ln_out != nullptr) {
-      __shared__ int s_last;
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        __threadfence();
-        const int n_tiles = (L.n + kRU - 1) / kRU;
-        const unsigned prev = atomicAdd(a.ln_cnt + m0 / kMTile, 1u);
-        s_last = (prev == (unsigned)(n_tiles * CL - 1));
-        if (s_last) {
-          __threadfence();
-          a.ln_cnt[m0 / kMTile] = 0u;
+    if (active) {
+      const uint32_t pbase = sbase + sm.p;
+      for (int i = threadIdx.x; i < RPR * 16; i += kThreads) {
+        const int row = i >> 4, c4 = i & 15;
+        if (4 * c4 < JT * 8) {
+          const uint32_t off = (uint32_t)(((r * RPR + row) * kPS + 4 * c4) * 4);
+          float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int q = 0; q < S; ++q) {
+            const float4 v = ld_dsmem_f4(mapa(pbase + off, (uint32_t)(sub0 + q)));
+            sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+          }
+          E[(4 * c4 + 0) * RPR + row] = sum.x;
+          E[(4 * c4 + 1) * RPR + row] = sum.y;
+          E[(4 * c4 + 2) * RPR + row] = sum.z;
+          E[(4 * c4 + 3) * RPR + row] = sum.w;
         }
       }
       __syncthreads();
-      if (s_last)
-        norm_rows<T>(reinterpret_cast<const T*>(a.out), a.ldo, m0, mrows, L.n,
-                     reinterpret_cast<const T*>(a.ln_w), reinterpret_cast<const T*>(a.ln_b),
-                     a.norm_kind, a.eps, reinterpret_cast<T*>(a.ln_out), a.ldo,
-                     reinterpret_cast<float*>(smem + sm.x));
+
+      // 7. epilogue on 8-column chunks: bias, round, GELU / residual, one
+      //    16-byte store per chunk (scalar stores for a ragged end)
+      T* out = reinterpret_cast<T*>(a.out);
+      const int cpt = RPR / 8;  // chunks per token row
+      const bool vec = (a.ldo % 8) == 0;
+      for (int i = threadIdx.x; i < mrows * cpt; i += kThreads) {
+        const int tok = i / cpt, ch = i - tok * cpt;
+        const int n0 = nbase + 8 * ch;
+        float v[8];
+        uint4 rq = make_uint4(0, 0, 0, 0);
+        if (a.epi == EPI_RESID) rq = *reinterpret_cast<const uint4*>(sres + tok * RPR + 8 * ch);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float y = Act<T>::round(E[tok * RPR + 8 * ch + e] + sbias[8 * ch + e]);
+          if (a.epi == EPI_GELU) {
+            y = Act<T>::round(gelu_erf(y));
+          } else if (a.epi == EPI_RESID) {
+            const float2 rf = Act<T>::unpack2(comp(rq, e >> 1));
+            y = Act<T>::round(((e & 1) ? rf.y : rf.x) + y);
+          }
+          v[e] = n0 + e < L.n ? y : 0.f;
+          E[tok * RPR + 8 * ch + e] = v[e];  // final values for the row statistics
+        }
+        T* dst = out + (size_t)(m0 + tok) * a.ldo + n0;
+        if (vec && n0 + 8 <= L.n) {
+          *reinterpret_cast<uint4*>(dst) = make_uint4(Act<T>::pack2(v[0], v[1]), Act<T>::pack2(v[2], v[3]),
+                                                      Act<T>::pack2(v[4], v[5]), Act<T>::pack2(v[6], v[7]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (n0 + e < L.n) dst[e] = Act<T>::from_f(v[e]);
+        }
+      }
+      if (a.out_stats) {
+        __syncthreads();
+        if (threadIdx.x < mrows) {  // this CTA's columns of one row, in column order
+          float sx = 0.f, sxx = 0.f;
+          for (int col = 0; col < RPR; ++col) {
+            const float y = E[threadIdx.x * RPR + col];
+            sx += y;
+            sxx += y * y;
+          }
+          ost[2 * threadIdx.x] = sx;
+          ost[2 * threadIdx.x + 1] = sxx;
+        }
+      }
+    }
+    cluster_sync();  // peers are done with this CTA's P; the partial stats are complete
+
+    // 8. the sub-cluster's first CTA combines the row statistics of its unit
+    if (active && a.out_stats && r == 0 && threadIdx.x < mrows) {
+      const uint32_t obase = sbase + sm.aux + kAuxOst + threadIdx.x * 8;
+      float sx = 0.f, sxx = 0.f;
+      for (int q = 0; q < S; ++q) {  // rank order: deterministic
+        const uint32_t ad = mapa(obase, (uint32_t)(sub0 + q));
+        sx += ld_dsmem_f32(ad);
+        sxx += ld_dsmem_f32(ad + 4);
+      }
+      float* st = a.out_stats + 2 * ((size_t)(m0 + threadIdx.x) * a.stat_slots + nt);
+      st[0] = sx;
+      st[1] = sxx;
     }
     __syncthreads();  // shared memory reuse by the next unit
   }
 
-  // Issue the prefetch of this CTA's first k-block of unit (cluster id) `u`.
-  static EE_DEV void prefetch_unit(const GemmArgs& a, int u, char* smem, const GemmSmem& sm,
-                                   PreRegs& pr) {
+  // All units of a GEMM in rounds over the cluster slots; `pre` applies to
+  // this CTA's first unit.
+  static EE_DEV void run(const GemmArgs& a, char* smem, const GemmSmem& sm, const PreRegs* pre) {
     const int n_tiles = (a.w.n + kRU - 1) / kRU;
-    const int nt = u % n_tiles;
-    const int CL = (int)cl_size(), rank = (int)cl_rank();
-    const int KB = a.w.k / CL / kKBlock;
-    prefetch(a.w, nt * kRU + 16 * (threadIdx.x >> 5), rank * KB, smem_u32(smem) + sm.pre, pr);
+    const int units = n_tiles * ((a.M + kMTile - 1) / kMTile);
+    const int per_cluster = (int)cl_size() >> a.lsplit;
+    const int slots = (int)cl_count() * per_cluster;
+    const int slot = (int)cl_id() * per_cluster + ((int)cl_rank() >> a.lsplit);
+    const int rounds = (units + slots - 1) / slots;
+    for (int rd = 0; rd < rounds; ++rd) {
+      const int u = rd * slots + slot;
+      const bool act = u < units;
+      unit(a, act, act ? u % n_tiles : 0, act ? (u / n_tiles) * kMTile : 0, smem, sm,
+           (rd == 0 && act) ? pre : nullptr);
+    }
+  }
+  // Start the prefetch of this CTA's first unit; returns whether it has one.
+  static EE_DEV bool start_prefetch(const GemmArgs& a, const GemmSmem& sm, char* smem, PreRegs& pr) {
+    const int n_tiles = (a.w.n + kRU - 1) / kRU;
+    const int units = n_tiles * ((a.M + kMTile - 1) / kMTile);
+    const int per_cluster = (int)cl_size() >> a.lsplit;
+    const int slot = (int)cl_id() * per_cluster + ((int)cl_rank() >> a.lsplit);
+    if (slot >= units || sm.pre_bytes < pre_kb_bytes(KIND)) return false;
+    prefetch(a, slot % n_tiles, sm, smem_u32(smem), pr);
+    return true;
   }
 };
 

@@ -35,10 +35,9 @@ __global__ void unpack_int4_kernel(const uint8_t* __restrict__ packed, int8_t* _
 // ---------------------------------------------------------------------------
 template <typename T, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
-    wq_gemm_kernel(const __grid_constant__ GemmArgs a, GemmSmem sm, int n_tiles, int units) {
+    wq_gemm_kernel(const __grid_constant__ GemmArgs a, GemmSmem sm) {
   extern __shared__ __align__(128) char smem[];
-  for (int u = (int)cl_id(); u < units; u += (int)cl_count())
-    Gemm<T, KIND>::unit(a, u % n_tiles, (u / n_tiles) * kMTile, smem, sm, nullptr);
+  Gemm<T, KIND>::run(a, smem, sm, nullptr);
 }
 
 // largest cluster (<= 8) whose K slices are whole 128-wide k-blocks
@@ -50,8 +49,10 @@ static int gemm_cluster(int k) {
 }
 
 template <typename T, int KIND>
-static int launch_gemm_k(const GemmArgs& a, cudaStream_t s) {
+static int launch_gemm_k(GemmArgs a, cudaStream_t s) {
   const int cl = gemm_cluster(a.w.k);
+  a.split = cl;
+  a.lsplit = cl == 8 ? 3 : (cl == 4 ? 2 : (cl == 2 ? 1 : 0));
   const int n_tiles = (a.w.n + kRU - 1) / kRU;
   const int m_tiles = (a.M + kMTile - 1) / kMTile;
   const long long units = (long long)n_tiles * m_tiles;
@@ -64,13 +65,19 @@ static int launch_gemm_k(const GemmArgs& a, cudaStream_t s) {
   GemmSmem sm;
   sm.x = 0;
   sm.p = (uint32_t)x;
-  sm.pre = (uint32_t)(x + kPBytes);
-  const size_t smem = sm.pre;
-  if (smem > 227 * 1024) return EE_ERR_UNSUPPORTED;
+  sm.aux = (uint32_t)(x + kPBytes);
+  sm.pre = (uint32_t)(sm.aux + kAuxBytes);
+  // stage the unit's weights with cp.async (up to 64 KB of k-blocks)
+  const size_t kbs = (size_t)(a.w.k / cl / kKBlock) * pre_kb_bytes(KIND);
+  sm.pre_bytes = (uint32_t)(kbs < 65536 ? kbs : (65536 / pre_kb_bytes(KIND)) * pre_kb_bytes(KIND));
+  const size_t smem = sm.pre + sm.pre_bytes;
+  const DevProps* dp = device_props();
+  if (!dp || smem + 1024 > (size_t)dp->smem_optin) return EE_ERR_UNSUPPORTED;
   auto fn = wq_gemm_kernel<T, KIND>;
   static std::atomic<int> smem_set[64];
   allow_max_smem(fn, smem_set);
-  const long long max_clusters = 65535LL * 4;
+  // one cluster per unit, at most 2^18 clusters (rounds beyond that)
+  const long long max_clusters = 1LL << 18;
   const long long nclus = units < max_clusters ? units : max_clusters;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)(nclus * cl));
@@ -84,7 +91,7 @@ static int launch_gemm_k(const GemmArgs& a, cudaStream_t s) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, fn, a, sm, n_tiles, (int)units);
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, fn, a, sm);
   return err == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
 }
 
@@ -106,10 +113,10 @@ using namespace ee;
 extern "C" {
 
 int ee_pack_int4(const int8_t* q, uint8_t* packed, int64_t n, int64_t k, ee_stream_t stream) {
-  if (!q || !packed) return EE_ERR_ARG;
   if (n < 0 || k < 0 || (k & 1)) return EE_ERR_SHAPE;
   const long long nbytes = (long long)n * (k / 2);
   if (nbytes == 0) return EE_OK;
+  if (!q || !packed) return EE_ERR_ARG;
   int rc = check_device();
   if (rc) return rc;
   const int grid = (int)((nbytes + 255) / 256 < 65536 ? (nbytes + 255) / 256 : 65536);
@@ -118,10 +125,10 @@ int ee_pack_int4(const int8_t* q, uint8_t* packed, int64_t n, int64_t k, ee_stre
 }
 
 int ee_unpack_int4(const uint8_t* packed, int8_t* q, int64_t n, int64_t k, ee_stream_t stream) {
-  if (!q || !packed) return EE_ERR_ARG;
   if (n < 0 || k < 0 || (k & 1)) return EE_ERR_SHAPE;
   const long long nbytes = (long long)n * (k / 2);
   if (nbytes == 0) return EE_OK;
+  if (!q || !packed) return EE_ERR_ARG;
   int rc = check_device();
   if (rc) return rc;
   const int grid = (int)((nbytes + 255) / 256 < 65536 ? (nbytes + 255) / 256 : 65536);
@@ -140,6 +147,7 @@ int ee_wq_gemm(const void* x, const void* weight, const void* scales, const void
   if ((epilogue & EE_EPI_GELU) && (epilogue & EE_EPI_RESIDUAL)) return EE_ERR_ARG;
   if ((epilogue & EE_EPI_BIAS) && !bias) return EE_ERR_ARG;
   if ((epilogue & EE_EPI_RESIDUAL) && !residual) return EE_ERR_ARG;
+  if ((epilogue & EE_EPI_RESIDUAL) && (n % 8) != 0) return EE_ERR_SHAPE;
   if (m < 1 || n < 1 || k < kKBlock || (k % kKBlock) != 0) return EE_ERR_SHAPE;
   if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) return EE_ERR_SHAPE;
   ee_linear L{};
@@ -169,7 +177,6 @@ int ee_wq_gemm(const void* x, const void* weight, const void* scales, const void
   a.resid = residual;
   a.ldr = n;
   a.has_bias = (epilogue & EE_EPI_BIAS) ? 1 : 0;
-  a.ln_out = nullptr;
   cudaStream_t s = (cudaStream_t)stream;
   return act_dtype == EE_BF16 ? launch_gemm_d<__nv_bfloat16>(a, s) : launch_gemm_d<__half>(a, s);
 }

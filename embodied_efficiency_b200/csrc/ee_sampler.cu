@@ -3,10 +3,14 @@
 #include "ee_sampler.cuh"
 
 namespace ee {
-extern template int launch_sampler<__nv_bfloat16, 64>(const Ctx&, cudaStream_t);
-extern template int launch_sampler<__nv_bfloat16, 128>(const Ctx&, cudaStream_t);
-extern template int launch_sampler<__half, 64>(const Ctx&, cudaStream_t);
-extern template int launch_sampler<__half, 128>(const Ctx&, cudaStream_t);
+extern template int launch_sampler<__nv_bfloat16, 64>(Ctx, cudaStream_t);
+extern template int launch_sampler<__nv_bfloat16, 128>(Ctx, cudaStream_t);
+extern template int launch_sampler<__half, 64>(Ctx, cudaStream_t);
+extern template int launch_sampler<__half, 128>(Ctx, cudaStream_t);
+extern template int sampler_geometry<__nv_bfloat16, 64>(const Ctx&, int*, int*, size_t*);
+extern template int sampler_geometry<__nv_bfloat16, 128>(const Ctx&, int*, int*, size_t*);
+extern template int sampler_geometry<__half, 64>(const Ctx&, int*, int*, size_t*);
+extern template int sampler_geometry<__half, 128>(const Ctx&, int*, int*, size_t*);
 
 // Self-test of the bounded grid barrier: CTA 1 leaves without arriving, so
 // CTA 0's wait can only end by its time limit.
@@ -37,6 +41,18 @@ size_t ee_flow_sample_workspace_bytes(const ee_expert* ex, int32_t n_steps) {
 int ee_flow_sample(const ee_expert* exp, const void* x_in, const void* t0, void* x_out,
                    int32_t n_steps, int32_t mode, void* workspace, size_t workspace_bytes,
                    ee_stream_t stream) {
+  return ee_flow_sample_traced(exp, x_in, t0, x_out, n_steps, mode, workspace, workspace_bytes,
+                               nullptr, stream);
+}
+
+int32_t ee_flow_sample_phases(const ee_expert* ex, int32_t n_steps) {
+  if (!ex || n_steps < 1 || ex->n_layers < 1) return 0;
+  return 3 + n_steps * (ex->n_layers * (ex->self_attn ? 8 : 5) + 1);
+}
+
+int ee_flow_sample_traced(const ee_expert* exp, const void* x_in, const void* t0, void* x_out,
+                          int32_t n_steps, int32_t mode, void* workspace, size_t workspace_bytes,
+                          uint64_t* trace, ee_stream_t stream) {
   if (!exp || !x_in || !x_out) return EE_ERR_ARG;
   const ee_expert& ex = *exp;
   int rc = validate_expert(ex, n_steps, mode);
@@ -64,16 +80,24 @@ int ee_flow_sample(const ee_expert* exp, const void* x_in, const void* t0, void*
   c.bar = reinterpret_cast<unsigned*>(ws + L.sync);
   c.abort_flag = reinterpret_cast<int*>(ws + L.sync + 4);
   c.status = reinterpret_cast<int*>(ws + L.sync + 8);
-  c.ln_cnt = reinterpret_cast<unsigned*>(ws + L.lncnt);
+  c.stats = reinterpret_cast<float*>(ws + L.stats);
+  c.n_inst = L.n_inst;
+  c.n_slots = L.n_slots;
+  c.ks_cap = sampler_ks_cap(ex);
   c.x = ws + L.x;
-  c.h = ws + L.h;
   c.qkv = ws + L.qkv;
   c.att = ws + L.att;
   c.qb = ws + L.qb;
   c.hid = ws + L.hid;
   c.emb = ws + L.emb;
   c.temb = ws + L.temb;
-  c.sm = sampler_smem_map(ex, sampler_cluster(ex));
+  {
+    const SamplerSmem sm = sampler_smem_map(ex, device_props()->smem_optin);
+    c.sm = sm.g;
+    c.desc = sm.desc;
+    c.smem_bytes = sm.total;
+  }
+  c.trace = reinterpret_cast<unsigned long long*>(trace);
 
   cudaStream_t s = (cudaStream_t)stream;
   if (cudaMemsetAsync(ws, 0, L.x, s) != cudaSuccess) return EE_ERR_LAUNCH;
@@ -81,6 +105,35 @@ int ee_flow_sample(const ee_expert* exp, const void* x_in, const void* t0, void*
   if (ex.act_dtype == EE_BF16)
     return hd == 64 ? launch_sampler<__nv_bfloat16, 64>(c, s) : launch_sampler<__nv_bfloat16, 128>(c, s);
   return hd == 64 ? launch_sampler<__half, 64>(c, s) : launch_sampler<__half, 128>(c, s);
+}
+
+int ee_flow_sample_geometry(const ee_expert* exp, int32_t* grid_ctas, int32_t* cluster,
+                            size_t* smem_bytes) {
+  if (!exp || !grid_ctas || !cluster || !smem_bytes) return EE_ERR_ARG;
+  int rc = check_device();
+  if (rc) return rc;
+  Ctx c{};
+  c.ex = *exp;
+  c.ks_cap = sampler_ks_cap(c.ex);
+  {
+    const SamplerSmem sm = sampler_smem_map(c.ex, device_props()->smem_optin);
+    c.sm = sm.g;
+    c.desc = sm.desc;
+    c.smem_bytes = sm.total;
+  }
+  int g = 0, cl = 0;
+  size_t sm = 0;
+  const int hd = c.ex.d_model / (c.ex.n_heads > 0 ? c.ex.n_heads : 1);
+  if (c.ex.act_dtype == EE_BF16)
+    rc = hd == 64 ? sampler_geometry<__nv_bfloat16, 64>(c, &g, &cl, &sm)
+                  : sampler_geometry<__nv_bfloat16, 128>(c, &g, &cl, &sm);
+  else
+    rc = hd == 64 ? sampler_geometry<__half, 64>(c, &g, &cl, &sm)
+                  : sampler_geometry<__half, 128>(c, &g, &cl, &sm);
+  *grid_ctas = g;
+  *cluster = cl;
+  *smem_bytes = sm;
+  return rc;
 }
 
 int ee_read_status(const void* workspace, int32_t* status, ee_stream_t stream) {

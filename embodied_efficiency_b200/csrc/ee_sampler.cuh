@@ -2,23 +2,28 @@
 // sampler call (kernel/flow_expert.py:127-137 flow_sample over
 // ActionExpert.forward :117-124 and Block.forward :83-95).
 //
-// One CTA per SM in clusters of CL CTAs, cooperative launch. A call is a
+// One CTA per SM in clusters of CL CTAs (cooperative launch). A call is a
 // fixed sequence of phases separated by a bounded grid barrier:
 //   EMB      time embedding of every step's t (t advanced in the act dtype)
 //   TPROJ    t_proj over all steps' embeddings at once (t does not depend on x)
-//   HEAD     step-0 in_proj + t_proj add + first norm (row-local, warp/token)
-//   per step, per block: qkv | self-attn | proj+residual(+norm) | q_c |
-//            cross-attn | out_c+residual(+norm) | mlp0+GELU | mlp2+residual(+norm)
+//   HEAD     step-0 in_proj + t_proj add (one CTA per token)
+//   per step, per block:
+//            qkv (first norm on load) | self-attn | proj + residual |
+//            q_c (norm on load) | cross-attn | out_c + residual |
+//            mlp0 (norm on load) + GELU | mlp2 + residual
 //   TAILHEAD out_norm + out_proj + Euler update of step k, then in_proj + t add
-//            + first norm of step k+1 (all row-local: one warp per token)
+//            of step k+1 (one CTA per token)
 //   TAIL     the last step's out_norm + out_proj + Euler update
-// GEMM phases are cluster split-K units (ee_gemm.cuh). Before each barrier a
-// CTA starts copying the weights of its first unit of the next GEMM phase
-// into shared memory, so weight latency overlaps the barrier. The norm after
-// a residual update is done by the last CTA to finish each 64-token tile.
+// GEMM phases are cluster split-K units (ee_gemm.cuh). The norms in front of
+// qkv / q_c / mlp0 are applied while those GEMMs stage their activation
+// slices, from per-token (sum, sum of squares) that the producing residual
+// phase accumulates atomically in its epilogue. Before each barrier a CTA
+// starts copying the weights of its first unit of the next GEMM phase into
+// shared memory, so weight latency overlaps the barrier.
 #pragma once
 
 #include <atomic>
+#include <mutex>
 
 #include "ee_attn.cuh"
 #include "ee_gemm.cuh"
@@ -39,9 +44,16 @@ struct Ctx {
   unsigned* bar;
   int* abort_flag;
   int* status;
-  unsigned* ln_cnt;
-  void *x, *h, *qkv, *att, *qb, *hid, *emb, *temb;
+  float* stats;  // [2 step parities][n_inst][M][n_slots][2] row (sum, sum of squares)
+  int n_inst;    // norms per step (3 per block, 2 without self-attention)
+  int n_slots;   // partial-statistics slots per row: 128-column tiles of d
+  uint32_t desc; // shared-memory copy of the block table (byte offset)
+  int ks_cap;    // largest K slice a GEMM unit may stage
+  int lsplit[7]; // log2 CTAs per unit of t_proj, qkv, proj, q_c, out_c, mlp0, mlp2
+  void *x, *qkv, *att, *qb, *hid, *emb, *temb;
   GemmSmem sm;
+  size_t smem_bytes;
+  unsigned long long* trace;  // optional [n_phases][grid][2] globaltimer stamps
 };
 
 struct Phase {
@@ -73,18 +85,21 @@ EE_DEV Phase decode(const Ctx& c, int p) {
   return ph;
 }
 
-// first norm of a block: n1, or nx when the block has no self-attention
-EE_DEV ee_norm first_norm(const Ctx& c, const ee_block* blk) {
-  return c.ex.self_attn ? blk->n1 : blk->nx;
+// norm instances of a step: first norm of layer l, nx of l, n2 of l
+EE_DEV int inst_first(const Ctx& c, int l) { return l * (c.ex.self_attn ? 3 : 2); }
+EE_DEV int inst_x(const Ctx& c, int l) { return c.ex.self_attn ? 3 * l + 1 : 2 * l; }
+EE_DEV int inst_2(const Ctx& c, int l) { return c.ex.self_attn ? 3 * l + 2 : 2 * l + 1; }
+EE_DEV float* stats_of(const Ctx& c, int step, int inst) {
+  return c.stats + ((size_t)((step & 1) * c.n_inst + inst) * c.M) * c.n_slots * 2;
 }
 
-EE_DEV GemmArgs make_gemm(const Ctx& c, const Phase& ph) {
+EE_DEV GemmArgs make_gemm(const Ctx& c, const Phase& ph, const char* smem) {
   GemmArgs a{};
   const int d = c.ex.d_model;
-  a.norm_kind = c.ex.norm_kind;
-  a.eps = c.ex.eps;
-  a.ln_cnt = c.ln_cnt;
   a.M = c.M;
+  a.stat_slots = c.n_slots;
+  a.in_norm = c.ex.norm_kind;
+  a.in_eps = c.ex.eps;
   if (ph.type == PH_TPROJ) {
     a.x = c.emb; a.ldx = d;
     a.w = c.ex.t_proj;
@@ -92,240 +107,219 @@ EE_DEV GemmArgs make_gemm(const Ctx& c, const Phase& ph) {
     a.epi = EPI_STORE;
     a.out = c.temb; a.ldo = d;
   } else {
-    const ee_block* blk = c.ex.blocks + ph.layer;
+    const ee_block* blk = reinterpret_cast<const ee_block*>(smem + c.desc) + ph.layer;
+    const int l = ph.layer;
     switch (ph.sub) {
       case 0:
-        a.x = c.h; a.ldx = d; a.w = blk->qkv; a.epi = EPI_STORE; a.out = c.qkv; a.ldo = 3 * d;
+        a.x = c.x; a.ldx = d; a.w = blk->qkv; a.epi = EPI_STORE; a.out = c.qkv; a.ldo = 3 * d;
+        a.in_stats = stats_of(c, ph.step, inst_first(c, l));
+        a.in_w = blk->n1.weight; a.in_b = blk->n1.bias;
         break;
       case 2:
         a.x = c.att; a.ldx = d; a.w = blk->proj; a.epi = EPI_RESID; a.out = c.x; a.ldo = d;
-        a.ln_w = blk->nx.weight; a.ln_b = blk->nx.bias; a.ln_out = c.h;
+        a.out_stats = stats_of(c, ph.step, inst_x(c, l));
         break;
       case 3:
-        a.x = c.h; a.ldx = d; a.w = blk->q_c; a.epi = EPI_STORE; a.out = c.qb; a.ldo = d;
+        a.x = c.x; a.ldx = d; a.w = blk->q_c; a.epi = EPI_STORE; a.out = c.qb; a.ldo = d;
+        a.in_stats = stats_of(c, ph.step, inst_x(c, l));
+        a.in_w = blk->nx.weight; a.in_b = blk->nx.bias;
         break;
       case 5:
         a.x = c.att; a.ldx = d; a.w = blk->out_c; a.epi = EPI_RESID; a.out = c.x; a.ldo = d;
-        a.ln_w = blk->n2.weight; a.ln_b = blk->n2.bias; a.ln_out = c.h;
+        a.out_stats = stats_of(c, ph.step, inst_2(c, l));
         break;
       case 6:
-        a.x = c.h; a.ldx = d; a.w = blk->mlp0; a.epi = EPI_GELU; a.out = c.hid; a.ldo = c.ex.hidden;
+        a.x = c.x; a.ldx = d; a.w = blk->mlp0; a.epi = EPI_GELU; a.out = c.hid; a.ldo = c.ex.hidden;
+        a.in_stats = stats_of(c, ph.step, inst_2(c, l));
+        a.in_w = blk->n2.weight; a.in_b = blk->n2.bias;
         break;
-      default: {  // 7
+      default:  // 7
         a.x = c.hid; a.ldx = c.ex.hidden; a.w = blk->mlp2; a.epi = EPI_RESID; a.out = c.x; a.ldo = d;
-        if (ph.layer + 1 < c.ex.n_layers) {
-          const ee_norm nn = first_norm(c, blk + 1);
-          a.ln_w = nn.weight; a.ln_b = nn.bias; a.ln_out = c.h;
-        }
-      }
+        if (l + 1 < c.ex.n_layers) a.out_stats = stats_of(c, ph.step, inst_first(c, l + 1));
     }
     if (a.epi == EPI_RESID) { a.resid = c.x; a.ldr = d; }
   }
   a.has_bias = a.w.bias != nullptr;
+  const int gi = ph.type == PH_TPROJ ? 0 : (ph.sub == 0 ? 1 : ph.sub == 2 ? 2 : ph.sub == 3 ? 3 : ph.sub == 5 ? 4 : ph.sub == 6 ? 5 : 6);
+  a.lsplit = c.lsplit[gi];
+  a.split = 1 << a.lsplit;
   return a;
 }
 
-EE_DEV int gemm_units(const GemmArgs& a) {
-  return ((a.w.n + kRU - 1) / kRU) * ((a.M + kMTile - 1) / kMTile);
-}
-
-template <typename T, int KIND>
-EE_DEV void gemm_phase_t(const GemmArgs& a, char* smem, const GemmSmem& sm, const PreRegs* pre,
-                         bool prefetch, PreRegs* pr_out) {
-  const int units = gemm_units(a);
-  const int n_tiles = (a.w.n + kRU - 1) / kRU;
-  if (prefetch) {
-    if ((int)cl_id() < units) Gemm<T, KIND>::prefetch_unit(a, cl_id(), smem, sm, *pr_out);
-    return;
-  }
-  const PreRegs* p = pre;
-  for (int u = cl_id(); u < units; u += cl_count()) {
-    Gemm<T, KIND>::unit(a, u % n_tiles, (u / n_tiles) * kMTile, smem, sm, p);
-    p = nullptr;
-  }
-}
-
-// run a GEMM phase (prefetch == false) or start the prefetch of this CTA's
-// first unit (prefetch == true; returns whether one was started)
+// run a GEMM phase, or (prefetch) start copying this CTA's first unit's
+// weights and return whether one was started
 template <typename T>
 EE_DEV bool gemm_dispatch(const GemmArgs& a, char* smem, const GemmSmem& sm, const PreRegs* pre,
                           bool prefetch, PreRegs* pr_out) {
   switch (a.w.wkind) {
-    case EE_W_DENSE: gemm_phase_t<T, EE_W_DENSE>(a, smem, sm, pre, prefetch, pr_out); break;
-    case EE_W_INT8: gemm_phase_t<T, EE_W_INT8>(a, smem, sm, pre, prefetch, pr_out); break;
-    case EE_W_INT4: gemm_phase_t<T, EE_W_INT4>(a, smem, sm, pre, prefetch, pr_out); break;
-    default: gemm_phase_t<T, EE_W_UINT4Z>(a, smem, sm, pre, prefetch, pr_out); break;
+    case EE_W_DENSE:
+      if (prefetch) return Gemm<T, EE_W_DENSE>::start_prefetch(a, sm, smem, *pr_out);
+      Gemm<T, EE_W_DENSE>::run(a, smem, sm, pre);
+      break;
+    case EE_W_INT8:
+      if (prefetch) return Gemm<T, EE_W_INT8>::start_prefetch(a, sm, smem, *pr_out);
+      Gemm<T, EE_W_INT8>::run(a, smem, sm, pre);
+      break;
+    case EE_W_INT4:
+      if (prefetch) return Gemm<T, EE_W_INT4>::start_prefetch(a, sm, smem, *pr_out);
+      Gemm<T, EE_W_INT4>::run(a, smem, sm, pre);
+      break;
+    default:
+      if (prefetch) return Gemm<T, EE_W_UINT4Z>::start_prefetch(a, sm, smem, *pr_out);
+      Gemm<T, EE_W_UINT4Z>::run(a, smem, sm, pre);
   }
-  return prefetch && (int)cl_id() < gemm_units(a);
+  return false;
 }
 
 // ---------------------------------------------------------------------------
-// row-local phases: one warp per token row, row staged in rb (d floats)
+// row-local phases: one CTA per token row
 // ---------------------------------------------------------------------------
-// norm of the row in rb; result stored to orow (T) when given, else written
-// back into rb rounded to the act dtype
-template <typename T>
-EE_DEV void norm_buf(float* rb, int d, const ee_norm& nrm, int kind, float eps, T* orow) {
-  const int lane = threadIdx.x & 31;
-  const float inv_d = 1.0f / (float)d;
-  const T* w = reinterpret_cast<const T*>(nrm.weight);
-  const T* b = reinterpret_cast<const T*>(nrm.bias);
-  __syncwarp();
-  float s = 0.f;
-  for (int i = lane; i < d; i += 32) s += kind == EE_NORM_RMS ? rb[i] * rb[i] : rb[i];
-  s = warp_sum(s);
-  float mean = 0.f, rstd;
-  if (kind == EE_NORM_RMS) {
-    rstd = 1.0f / sqrtf(s * inv_d + eps);
-  } else {
-    mean = s * inv_d;
-    float q = 0.f;
-    for (int i = lane; i < d; i += 32) q += (rb[i] - mean) * (rb[i] - mean);
-    rstd = 1.0f / sqrtf(warp_sum(q) * inv_d + eps);
-  }
-  for (int c = lane; c < d / 8; c += 32) {
-    const uint4 wq = __ldg(reinterpret_cast<const uint4*>(w + c * 8));
-    const uint4 bq = b ? __ldg(reinterpret_cast<const uint4*>(b + c * 8)) : make_uint4(0, 0, 0, 0);
-    float y[8];
+EE_DEV float block_sum(float v, float* scratch /* [kWarps] */) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = 0.f;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 wf = Act<T>::unpack2(comp(wq, e));
-      const float2 bf = Act<T>::unpack2(comp(bq, e));
-      const float v0 = rb[c * 8 + 2 * e], v1 = rb[c * 8 + 2 * e + 1];
-      if (kind == EE_NORM_RMS) {
-        y[2 * e] = Act<T>::round(v0 * rstd) * wf.x;
-        y[2 * e + 1] = Act<T>::round(v1 * rstd) * wf.y;
-      } else {
-        y[2 * e] = (v0 - mean) * rstd * wf.x + bf.x;
-        y[2 * e + 1] = (v1 - mean) * rstd * wf.y + bf.y;
+  for (int i = 0; i < kWarps; ++i) r += scratch[i];
+  __syncthreads();
+  return r;
+}
+
+// Token row m at `step`: (tail) out_norm + out_proj + Euler update or
+// velocity store, then (head) x = in_proj(x_act) + b + temb(next step) with
+// its row statistics for the next first norm. Shared memory: d + 48 floats.
+template <typename T>
+EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head, char* smem) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int d = c.ex.d_model, A = c.ex.action_dim, nch = d / 8;
+  float* hrow = reinterpret_cast<float*>(smem + c.sm.x);  // [d]
+  float* xa = hrow + d;                                    // [32]
+  float* red = xa + 32;                                    // [kWarps]
+  const int head_step = do_tail ? step + 1 : 0;
+  if (do_tail) {
+    // out_norm of x[m], rounded to the act dtype (the module output)
+    float v[8];
+    const T* xr = reinterpret_cast<const T*>(c.x) + (size_t)m * d;
+    float s = 0.f;
+    if (tid < nch) {
+      const uint4 q = ld_act16(xr + tid * 8);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = Act<T>::unpack2(comp(q, e));
+        v[2 * e] = f.x;
+        v[2 * e + 1] = f.y;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s += c.ex.norm_kind == EE_NORM_RMS ? v[e] * v[e] : v[e];
+    }
+    s = block_sum(s, red);
+    const float inv_d = 1.0f / (float)d;
+    float mean = 0.f, rstd;
+    if (c.ex.norm_kind == EE_NORM_RMS) {
+      rstd = 1.0f / sqrtf(s * inv_d + c.ex.eps);
+    } else {
+      mean = s * inv_d;
+      float q2 = 0.f;
+      if (tid < nch)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q2 += (v[e] - mean) * (v[e] - mean);
+      rstd = 1.0f / sqrtf(block_sum(q2, red) * inv_d + c.ex.eps);
+    }
+    if (tid < nch) {
+      const T* w = reinterpret_cast<const T*>(c.ex.out_norm.weight);
+      const T* b = reinterpret_cast<const T*>(c.ex.out_norm.bias);
+      const uint4 wq = __ldg(reinterpret_cast<const uint4*>(w + tid * 8));
+      const uint4 bq = b ? __ldg(reinterpret_cast<const uint4*>(b + tid * 8)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 wf = Act<T>::unpack2(comp(wq, e));
+        const float2 bf = Act<T>::unpack2(comp(bq, e));
+        float y0, y1;
+        if (c.ex.norm_kind == EE_NORM_RMS) {
+          y0 = Act<T>::round(v[2 * e] * rstd) * wf.x;
+          y1 = Act<T>::round(v[2 * e + 1] * rstd) * wf.y;
+        } else {
+          y0 = (v[2 * e] - mean) * rstd * wf.x + bf.x;
+          y1 = (v[2 * e + 1] - mean) * rstd * wf.y + bf.y;
+        }
+        hrow[tid * 8 + 2 * e] = Act<T>::round(y0);
+        hrow[tid * 8 + 2 * e + 1] = Act<T>::round(y1);
       }
     }
-    if (orow) {
-      *reinterpret_cast<uint4*>(orow + c * 8) =
-          make_uint4(Act<T>::pack2(y[0], y[1]), Act<T>::pack2(y[2], y[3]),
-                     Act<T>::pack2(y[4], y[5]), Act<T>::pack2(y[6], y[7]));
-    } else {
+    __syncthreads();
+    // out_proj: warp w computes outputs a = w, w+8, w+16, w+24
+    const T* W = reinterpret_cast<const T*>(c.ex.out_proj.weight);
+    const T* ob = reinterpret_cast<const T*>(c.ex.out_proj.bias);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) rb[c * 8 + e] = Act<T>::round(y[e]);
-    }
-  }
-  __syncwarp();
-}
-
-// x[m] = in_proj(x_act[m]) + b + temb(step); h[m] = first_norm(x[m]).
-// xa_lane: lane a (< action_dim) holds x_act[m][a].
-template <typename T>
-EE_DEV void head_row(const Ctx& c, int m, int step, float xa_lane, float* rb) {
-  const int lane = threadIdx.x & 31;
-  const int d = c.ex.d_model, A = c.ex.action_dim;
-  float xa[32];
+    for (int j = 0; j < 4; ++j) {
+      const int a = warp + kWarps * j;
+      if (a < A) {
+        float acc = 0.f;
+        for (int ch = lane; ch < nch; ch += 32) {
+          const uint4 wv = ld_weight16(W + (size_t)a * d + ch * 8);
 #pragma unroll
-  for (int a = 0; a < 32; ++a) xa[a] = __shfl_sync(0xffffffffu, xa_lane, a);
-  const int bb = m / c.ex.horizon;
-  const int trow = step * c.nbt + (c.nbt > 1 ? bb : 0);
-  const T* W = reinterpret_cast<const T*>(c.ex.in_proj.weight);
-  const T* bias = reinterpret_cast<const T*>(c.ex.in_proj.bias);
-  const T* temb = reinterpret_cast<const T*>(c.temb) + (size_t)trow * d;
-  T* xr = reinterpret_cast<T*>(c.x) + (size_t)m * d;
-  for (int ch = lane; ch < d / 8; ch += 32) {
-    const uint4 tq = ld_act16(temb + ch * 8);
-    float y[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int n = ch * 8 + e;
-      const T* wr = W + (size_t)n * A;
-      float acc = 0.f;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (q * 8 < A) {
-          const uint4 w = ld_weight16(wr + 8 * q);
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            const float2 f = Act<T>::unpack2(comp(w, cc));
-            acc = fmaf(xa[8 * q + 2 * cc], f.x, acc);
-            acc = fmaf(xa[8 * q + 2 * cc + 1], f.y, acc);
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = Act<T>::unpack2(comp(wv, e));
+            acc = fmaf(hrow[ch * 8 + 2 * e], f.x, acc);
+            acc = fmaf(hrow[ch * 8 + 2 * e + 1], f.y, acc);
+          }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) {
+          const float vel = Act<T>::round(acc + (ob ? ld_param(ob + a) : 0.f));
+          T* xo = reinterpret_cast<T*>(c.x_out) + (size_t)m * A + a;
+          if (c.mode == EE_MODE_VELOCITY) {
+            *xo = Act<T>::from_f(vel);
+          } else {
+            const T* src = step == 0 ? reinterpret_cast<const T*>(c.x_in) + (size_t)m * A + a : xo;
+            const float xnew = Act<T>::round(Act<T>::to_f(*src) + Act<T>::round(vel * c.dtf));
+            *xo = Act<T>::from_f(xnew);
+            xa[a] = xnew;
           }
         }
       }
-      if (bias) acc += ld_param(bias + n);
-      const float2 tf = Act<T>::unpack2(comp(tq, e >> 1));
-      y[e] = Act<T>::round(Act<T>::round(acc) + ((e & 1) ? tf.y : tf.x));
-      rb[n] = y[e];
     }
-    *reinterpret_cast<uint4*>(xr + ch * 8) =
-        make_uint4(Act<T>::pack2(y[0], y[1]), Act<T>::pack2(y[2], y[3]),
-                   Act<T>::pack2(y[4], y[5]), Act<T>::pack2(y[6], y[7]));
+  } else if (tid < A) {
+    xa[tid] = Act<T>::to_f(reinterpret_cast<const T*>(c.x_in)[(size_t)m * A + tid]);
   }
-  norm_buf<T>(rb, d, first_norm(c, c.ex.blocks), c.ex.norm_kind, c.ex.eps,
-              reinterpret_cast<T*>(c.h) + (size_t)m * d);
-}
-
-// out_norm + out_proj + Euler update (or velocity store) of token row m at
-// `step`; returns the new x_act value held by lane a (< action_dim).
-template <typename T>
-EE_DEV float tail_row(const Ctx& c, int m, int step, float* rb) {
-  const int lane = threadIdx.x & 31;
-  const int d = c.ex.d_model, A = c.ex.action_dim;
-  const T* xr = reinterpret_cast<const T*>(c.x) + (size_t)m * d;
-  for (int ch = lane; ch < d / 8; ch += 32) {
-    const uint4 q = ld_act16(xr + ch * 8);
+  if (!do_head) return;
+  __syncthreads();
+  // in_proj + bias + t_proj(temb) for the head step; row statistics
+  const int bb = m / c.ex.horizon;
+  const int trow = head_step * c.nbt + (c.nbt > 1 ? bb : 0);
+  const T* Wi = reinterpret_cast<const T*>(c.ex.in_proj.weight);
+  const T* bi = reinterpret_cast<const T*>(c.ex.in_proj.bias);
+  const T* temb = reinterpret_cast<const T*>(c.temb) + (size_t)trow * d;
+  T* xr = reinterpret_cast<T*>(c.x) + (size_t)m * d;
+  float s = 0.f, ss = 0.f;
+  for (int n = tid; n < d; n += kThreads) {
+    const T* wr = Wi + (size_t)n * A;
+    float acc = 0.f;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = Act<T>::unpack2(comp(q, e));
-      rb[ch * 8 + 2 * e] = f.x;
-      rb[ch * 8 + 2 * e + 1] = f.y;
-    }
-  }
-  norm_buf<T>(rb, d, c.ex.out_norm, c.ex.norm_kind, c.ex.eps, nullptr);
-  // out_proj partial dots of this lane's chunks for every output a
-  const T* W = reinterpret_cast<const T*>(c.ex.out_proj.weight);
-  float part[32];
+    for (int q = 0; q < 4; ++q) {
+      if (q * 8 < A) {
+        const uint4 wv = ld_weight16(wr + 8 * q);
 #pragma unroll
-  for (int a = 0; a < 32; ++a) part[a] = 0.f;
-  for (int ch = lane; ch < d / 8; ch += 32) {
-    float hv[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) hv[e] = rb[ch * 8 + e];
-#pragma unroll
-    for (int a = 0; a < 32; ++a) {
-      if (a < A) {
-        const uint4 w = ld_weight16(W + (size_t)a * d + ch * 8);
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const float2 f = Act<T>::unpack2(comp(w, cc));
-          part[a] = fmaf(hv[2 * cc], f.x, part[a]);
-          part[a] = fmaf(hv[2 * cc + 1], f.y, part[a]);
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = Act<T>::unpack2(comp(wv, e));
+          acc = fmaf(xa[8 * q + 2 * e], f.x, acc);
+          acc = fmaf(xa[8 * q + 2 * e + 1], f.y, acc);
         }
       }
     }
+    if (bi) acc += ld_param(bi + n);
+    const float y = Act<T>::round(Act<T>::round(acc) + ld_act_scalar(temb + n));
+    xr[n] = Act<T>::from_f(y);
+    s += y;
+    ss += y * y;
   }
-  // transpose-reduce: afterwards lane a holds the full sum of output a
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    const bool upper = (lane & o) != 0;
-#pragma unroll
-    for (int i = 0; i < o; ++i) {
-      const float send = upper ? part[i] : part[i + o];
-      const float keep = upper ? part[i + o] : part[i];
-      part[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-    }
+  s = block_sum(s, red);
+  ss = block_sum(ss, red);
+  if (tid == 0) {  // slot 0 holds the whole row (the other slots stay zero)
+    float* st = stats_of(c, head_step, 0) + 2 * (size_t)m * c.n_slots;
+    st[0] = s;
+    st[1] = ss;
   }
-  float xa_new = 0.f;
-  if (lane < A) {
-    const T* ob = reinterpret_cast<const T*>(c.ex.out_proj.bias);
-    const float vel = Act<T>::round(part[0] + (ob ? ld_param(ob + lane) : 0.f));
-    T* xo = reinterpret_cast<T*>(c.x_out) + (size_t)m * A + lane;
-    if (c.mode == EE_MODE_VELOCITY) {
-      *xo = Act<T>::from_f(vel);
-      xa_new = vel;
-    } else {
-      const T* src = step == 0 ? reinterpret_cast<const T*>(c.x_in) + (size_t)m * A + lane : xo;
-      const float xa_old = Act<T>::to_f(*src);
-      xa_new = Act<T>::round(xa_old + Act<T>::round(vel * c.dtf));
-      *xo = Act<T>::from_f(xa_new);
-    }
-  }
-  return xa_new;
 }
 
 // ---------------------------------------------------------------------------
@@ -373,15 +367,26 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
   PreRegs pre;
   bool have_pre = false;
   const int P = num_phases(c);
-  const int gwarp = blockIdx.x * kWarps + (threadIdx.x >> 5);
-  const int nwarps = gridDim.x * kWarps;
-  const int lane = threadIdx.x & 31;
   const int d = c.ex.d_model;
-  float* rb = reinterpret_cast<float*>(smem + c.sm.x) + (size_t)(threadIdx.x >> 5) * d;
   unsigned target = 0;
+  {  // block table -> shared memory (read by every GEMM phase)
+    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(c.ex.blocks);
+    unsigned long long* dst = reinterpret_cast<unsigned long long*>(smem + c.desc);
+    const int n = c.ex.n_layers * (int)(sizeof(ee_block) / 8);
+    for (int i = threadIdx.x; i < n; i += kThreads) dst[i] = src[i];
+    __syncthreads();
+  }
 
   for (int p = 0; p < P; ++p) {
     const Phase ph = decode(c, p);
+    // the first block phase of step k clears the statistics step k+1 uses
+    if ((ph.type == PH_GEMM || ph.type == PH_ATTN_SELF || ph.type == PH_ATTN_CROSS) &&
+        ph.layer == 0 && ph.sub == (c.ex.self_attn ? 0 : 3)) {
+      float* st = c.stats + (size_t)(((ph.step + 1) & 1) * c.n_inst) * c.M * c.n_slots * 2;
+      const size_t n = (size_t)c.n_inst * c.M * c.n_slots * 2;
+      for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += (size_t)gridDim.x * kThreads)
+        st[i] = 0.f;
+    }
     switch (ph.type) {
       case PH_EMB: {
         const int half = d / 2;
@@ -402,12 +407,12 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
       }
       case PH_TPROJ:
       case PH_GEMM:
-        gemm_dispatch<T>(make_gemm(c, ph), smem, c.sm, have_pre ? &pre : nullptr, false, nullptr);
+        gemm_dispatch<T>(make_gemm(c, ph, smem), smem, c.sm, have_pre ? &pre : nullptr, false, nullptr);
         break;
       case PH_ATTN_SELF:
       case PH_ATTN_CROSS: {
         AttnArgs at{};
-        const ee_block* blk = c.ex.blocks + ph.layer;
+        const ee_block* blk = reinterpret_cast<const ee_block*>(smem + c.desc) + ph.layer;
         if (ph.type == PH_ATTN_SELF) {
           const T* qkv = reinterpret_cast<const T*>(c.qkv);
           at.q = qkv; at.ldq = 3 * d;
@@ -433,36 +438,35 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
           Attn<T, HD>::unit(at, u / c.ex.n_heads, u % c.ex.n_heads, smem);
         break;
       }
-      case PH_HEAD: {
-        for (int m = gwarp; m < c.M; m += nwarps) {
-          const float xa =
-              lane < c.ex.action_dim
-                  ? Act<T>::to_f(reinterpret_cast<const T*>(c.x_in)[(size_t)m * c.ex.action_dim + lane])
-                  : 0.f;
-          head_row<T>(c, m, 0, xa, rb);
+      case PH_HEAD:
+        for (int m = blockIdx.x; m < c.M; m += gridDim.x) {
+          row_phase<T>(c, m, 0, false, true, smem);
+          __syncthreads();
         }
         break;
-      }
-      default: {  // PH_TAILHEAD, PH_TAIL
-        for (int m = gwarp; m < c.M; m += nwarps) {
-          const float xa = tail_row<T>(c, m, ph.step, rb);
-          if (ph.type == PH_TAILHEAD) head_row<T>(c, m, ph.step + 1, xa, rb);
+      default:  // PH_TAILHEAD, PH_TAIL
+        for (int m = blockIdx.x; m < c.M; m += gridDim.x) {
+          row_phase<T>(c, m, ph.step, true, ph.type == PH_TAILHEAD, smem);
+          __syncthreads();
         }
         break;
-      }
     }
     have_pre = false;
+    __syncthreads();  // this CTA is done with phase p (and its shared memory)
+    if (c.trace && threadIdx.x == 0)
+      c.trace[((size_t)p * gridDim.x + blockIdx.x) * 2] = globaltimer();
     if (p + 1 < P) {
       const Phase nx = decode(c, p + 1);
-      __syncthreads();  // this CTA is done with its shared memory for phase p
       if (nx.type == PH_GEMM || nx.type == PH_TPROJ)
-        have_pre = gemm_dispatch<T>(make_gemm(c, nx), smem, c.sm, nullptr, true, &pre);
+        have_pre = gemm_dispatch<T>(make_gemm(c, nx, smem), smem, c.sm, nullptr, true, &pre);
       target += gridDim.x;
       if (!grid_barrier(c, target)) {
         cp_async_wait<0>();
         return;
       }
     }
+    if (c.trace && threadIdx.x == 0)
+      c.trace[((size_t)p * gridDim.x + blockIdx.x) * 2 + 1] = globaltimer();
   }
 }
 
@@ -470,8 +474,8 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
 // host side
 // ---------------------------------------------------------------------------
 struct Layout {
-  size_t sync, lncnt, x, h, qkv, att, qb, hid, emb, temb, total;
-  int M, m_tiles, Rt_max;
+  size_t sync, stats, x, qkv, att, qb, hid, emb, temb, total;
+  int M, n_inst, n_slots, Rt_max;
 };
 
 inline size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -481,13 +485,13 @@ inline Layout layout_for(const ee_expert& ex, int n_steps) {
   const size_t e = 2;  // bytes per act element
   const size_t d = (size_t)ex.d_model;
   L.M = ex.batch * ex.horizon;
-  L.m_tiles = (L.M + kMTile - 1) / kMTile;
+  L.n_inst = ex.n_layers * (ex.self_attn ? 3 : 2);
   L.Rt_max = n_steps * ex.batch;
   size_t off = 0;
   L.sync = off; off += 256;
-  L.lncnt = off; off += al256((size_t)L.m_tiles * 4);
+  L.n_slots = (ex.d_model + kRU - 1) / kRU;
+  L.stats = off; off += al256((size_t)2 * L.n_inst * L.M * L.n_slots * 2 * sizeof(float));
   L.x = off; off += al256((size_t)L.M * d * e);
-  L.h = off; off += al256((size_t)L.M * d * e);
   L.qkv = off; off += ex.self_attn ? al256((size_t)L.M * 3 * d * e) : 0;
   L.att = off; off += al256((size_t)L.M * d * e);
   L.qb = off; off += al256((size_t)L.M * d * e);
@@ -498,8 +502,8 @@ inline Layout layout_for(const ee_expert& ex, int n_steps) {
   return L;
 }
 
-// cluster size of the sampler: every GEMM K (d and hidden) must split into
-// 128-wide slices
+// cluster size of the sampler: the model width must split into 128-wide
+// k-blocks across the cluster (K = d_model is the smallest GEMM K)
 inline int sampler_cluster(const ee_expert& ex) {
   const int kb = ex.d_model / 128;
   int cl = 8;
@@ -507,25 +511,43 @@ inline int sampler_cluster(const ee_expert& ex) {
   return cl;
 }
 
-inline GemmSmem sampler_smem_map(const ee_expert& ex, int cl) {
+// largest K slice a unit stages: what the widest GEMM (K = max(d, hidden))
+// needs with the whole cluster splitting it, at least 512
+inline int sampler_ks_cap(const ee_expert& ex) {
   const int kmax = ex.hidden > ex.d_model ? ex.hidden : ex.d_model;
-  size_t x = gemm_x_bytes(kmax / cl);
-  const size_t e = (size_t)kMTile * (kRU / cl) * 4;
-  const size_t rows = (size_t)kWarps * ex.d_model * 4;
-  if (e > x) x = e;
-  if (rows > x) x = rows;
-  x = (x + 127) & ~(size_t)127;
-  GemmSmem sm;
-  sm.x = 0;
-  sm.p = (uint32_t)x;
-  sm.pre = (uint32_t)(x + kPBytes);
-  return sm;
+  const int need = kmax / sampler_cluster(ex);
+  return need > 512 ? need : 512;
 }
 
-template <int HD>
-inline size_t sampler_smem_bytes(const GemmSmem& sm) {
-  const size_t g = (size_t)sm.pre + kPreBytes;
-  return g > (size_t)AttnSmem<HD>::kTotal ? g : (size_t)AttnSmem<HD>::kTotal;
+struct SamplerSmem {
+  GemmSmem g;
+  uint32_t desc;   // block table copy
+  size_t total;    // dynamic shared memory of the launch
+};
+
+inline SamplerSmem sampler_smem_map(const ee_expert& ex, int smem_optin) {
+  size_t x = gemm_x_bytes(sampler_ks_cap(ex));
+  if (x < (size_t)kMTile * kRU * 4) x = (size_t)kMTile * kRU * 4;  // reduced tile E
+  const size_t rows = ((size_t)ex.d_model + 64) * 4;                // row phases
+  if (rows > x) x = rows;
+  x = (x + 127) & ~(size_t)127;
+  SamplerSmem sm;
+  sm.g.x = 0;
+  sm.g.p = (uint32_t)x;
+  sm.g.aux = (uint32_t)(x + kPBytes);
+  // the block table must survive the attention phases, which use [0, attn)
+  const size_t hd = ex.n_heads > 0 ? ex.d_model / ex.n_heads : 64;
+  const size_t attn = hd == 128 ? AttnSmem<128>::kTotal : AttnSmem<64>::kTotal;
+  size_t desc = sm.g.aux + kAuxBytes;
+  if (desc < attn) desc = attn;
+  desc = (desc + 127) & ~(size_t)127;
+  sm.desc = (uint32_t)desc;
+  const size_t pre = (desc + (size_t)ex.n_layers * sizeof(ee_block) + 127) & ~(size_t)127;
+  sm.g.pre = (uint32_t)pre;
+  const long long room = (long long)smem_optin - 1024 - (long long)pre;  // 1 KB static reserve
+  sm.g.pre_bytes = room > 0 ? (uint32_t)(room < 128 * 1024 ? room : 128 * 1024) : 0;
+  sm.total = pre + sm.g.pre_bytes;
+  return sm;
 }
 
 inline int validate_expert(const ee_expert& ex, int n_steps, int mode) {
@@ -554,10 +576,9 @@ inline int validate_expert(const ee_expert& ex, int n_steps, int mode) {
   if (!aligned16(ex.in_proj.weight) || !aligned16(ex.out_proj.weight) ||
       !aligned16(ex.out_norm.weight) || (ex.out_norm.bias && !aligned16(ex.out_norm.bias)))
     return EE_ERR_ALIGN;
-  // shared memory must hold the largest GEMM slice
-  const int cl = sampler_cluster(ex);
-  const GemmSmem sm = sampler_smem_map(ex, cl);
-  if ((size_t)sm.pre + kPreBytes > 227 * 1024) return EE_ERR_UNSUPPORTED;
+  // shared memory must hold the widest GEMM slice next to the fixed regions
+  const SamplerSmem sm = sampler_smem_map(ex, 232448);
+  if ((size_t)sm.g.pre + 1024 > 232448) return EE_ERR_UNSUPPORTED;
   return validate_linear(ex.t_proj, ex.d_model, ex.d_model);
 }
 
@@ -587,13 +608,83 @@ inline int validate_blocks(const ee_expert& ex, const ee_block* hb) {
 }
 
 template <typename T, int HD>
-int launch_sampler(const Ctx& c, cudaStream_t s) {
+constexpr auto fn_of() { return sampler_kernel<T, HD>; }
+
+// Launch geometry of the sampler kernel: clusters of `cl` CTAs, as many as
+// can be resident at once (at most one CTA per SM).
+template <typename T, int HD>
+int sampler_geometry(const Ctx& c, int* grid, int* cl_out, size_t* smem_out) {
   auto fn = sampler_kernel<T, HD>;
   const int cl = sampler_cluster(c.ex);
-  const size_t smem = sampler_smem_bytes<HD>(c.sm);
+  const size_t smem = c.smem_bytes;
   static std::atomic<int> smem_set[64];
   allow_max_smem(fn, smem_set);
+  // the occupancy query is costly: remember the last answer per device
+  static std::mutex mu;
+  static struct { int cl; size_t smem; int grid; } memo[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return EE_ERR_DEVICE;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (memo[dev].grid > 0 && memo[dev].cl == cl && memo[dev].smem == smem) {
+      *grid = memo[dev].grid;
+      *cl_out = cl;
+      *smem_out = smem;
+      return EE_OK;
+    }
+  }
   cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(cl);
+  int nclusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&nclusters, fn, &cfg) != cudaSuccess || nclusters < 1)
+    return EE_ERR_LAUNCH;
+  const int max_ctas = device_sms();
+  if (nclusters * cl > max_ctas) nclusters = max_ctas / cl;
+  *grid = nclusters * cl;
+  *cl_out = cl;
+  *smem_out = smem;
+  std::lock_guard<std::mutex> g(mu);
+  memo[dev].cl = cl;
+  memo[dev].smem = smem;
+  memo[dev].grid = *grid;
+  return EE_OK;
+}
+
+// CTAs per unit of every GEMM of the step (host-side, from the grid geometry)
+inline int plan_splits(Ctx& c, int grid, int cl) {
+  const ee_expert& ex = c.ex;
+  const int d = ex.d_model, M = c.M;
+  const int shapes[7][3] = {{d, d, c.Rt}, {3 * d, d, M}, {d, d, M}, {d, d, M},
+                            {d, d, M}, {ex.hidden, d, M}, {d, ex.hidden, M}};
+  for (int i = 0; i < 7; ++i) {
+    const int sp = pick_split(shapes[i][0], shapes[i][1], shapes[i][2], grid / cl, cl, c.ks_cap);
+    if (sp <= 0) return EE_ERR_UNSUPPORTED;
+    int l = 0;
+    while ((1 << l) < sp) ++l;
+    c.lsplit[i] = l;
+  }
+  return EE_OK;
+}
+
+template <typename T, int HD>
+int launch_sampler(Ctx c, cudaStream_t s) {
+  int grid = 0, cl = 0;
+  size_t smem = 0;
+  int rc = sampler_geometry<T, HD>(c, &grid, &cl, &smem);
+  if (rc) return rc;
+  rc = plan_splits(c, grid, cl);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -605,22 +696,13 @@ int launch_sampler(const Ctx& c, cudaStream_t s) {
   attr[1].id = cudaLaunchAttributeCooperative;
   attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  // as many whole clusters as can be resident at once (one CTA per SM)
-  cfg.gridDim = dim3(cl);
-  int nclusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&nclusters, fn, &cfg) != cudaSuccess || nclusters < 1)
-    return EE_ERR_LAUNCH;
-  const int max_ctas = device_sms();
-  if (nclusters * cl > max_ctas) nclusters = max_ctas / cl;
-  cfg.gridDim = dim3(nclusters * cl);
   // Cooperative launch guarantees that every CTA is resident. Inside a stream
   // capture the plain cluster launch is used: the grid is sized to what can be
   // resident at once, and every barrier wait is bounded either way.
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(s, &cap) != cudaSuccess) return EE_ERR_LAUNCH;
   cfg.numAttrs = cap == cudaStreamCaptureStatusNone ? 2 : 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, c);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn_of<T, HD>(), c);
   return e == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
 }
 

@@ -212,6 +212,37 @@ class FusedPlan:
         _lib.check(rc, "ee_flow_sample")
         return out
 
+    def trace(self, x, n_steps: int):
+        """Run one call with the device phase timeline on; returns (phase kinds,
+        int64 tensor [n_phases, grid, 2] of globaltimer ns: work done, barrier left)."""
+        lib = _lib.load()
+        grid, _, _ = self.geometry()
+        nph = lib.ee_flow_sample_phases(ctypes.byref(self.ex), n_steps)
+        tr = torch.zeros(nph, grid, 2, dtype=torch.int64, device=self.device)
+        xin = x.to(self.act).contiguous()
+        out = torch.empty_like(xin)
+        ws = self.workspace(n_steps)
+        _lib.check(lib.ee_flow_sample_traced(ctypes.byref(self.ex), xin.data_ptr(), None,
+                                             out.data_ptr(), n_steps, _lib.EE_MODE_EULER,
+                                             ws.data_ptr(), ws.numel(), tr.data_ptr(),
+                                             _lib.stream_ptr(self.device)), "ee_flow_sample_traced")
+        torch.cuda.synchronize(self.device)
+        per_block = ["qkv", "self_attn", "proj", "q_c", "cross_attn", "out_c", "mlp0", "mlp2"]
+        if not self.self_attn:
+            per_block = per_block[3:]
+        kinds = ["emb", "t_proj", "head"]
+        for _ in range(n_steps):
+            kinds += per_block * self.cfg.n_layers + ["tail"]
+        return kinds, tr.cpu()
+
+    def geometry(self):
+        """(grid CTAs, CTAs per cluster, dynamic shared memory bytes) of the launch."""
+        g, c, sm = ctypes.c_int32(0), ctypes.c_int32(0), ctypes.c_size_t(0)
+        _lib.check(_lib.load().ee_flow_sample_geometry(ctypes.byref(self.ex), ctypes.byref(g),
+                                                       ctypes.byref(c), ctypes.byref(sm)),
+                   "ee_flow_sample_geometry")
+        return g.value, c.value, sm.value
+
     def status(self, n_steps: int) -> int:
         """Device status word of the last launch with ``n_steps`` (synchronises)."""
         st = ctypes.c_int32(0)

@@ -19,6 +19,8 @@
  *                         (mode EE_MODE_VELOCITY = one ActionExpert.forward)
  *   ee_flow_sample_workspace_bytes   sizing helper for ee_flow_sample (new)
  *   ee_check_expert       one-time validation of an expert description (new)
+ *   ee_flow_sample_geometry   launch geometry of the fused sampler (new)
+ *   ee_flow_sample_traced / ee_flow_sample_phases   per-phase device timeline (new)
  *   ee_read_status        device status word of a sampler workspace (new)
  *   ee_barrier_selftest   bounded-wait self-test of the grid barrier (new)
  *   ee_strerror / ee_version / ee_struct_size   (new)
@@ -131,6 +133,18 @@ typedef struct ee_expert {
   const ee_block* blocks; /* DEVICE pointer to n_layers ee_block records */
 } ee_expert;
 
+/* Tracing variant of ee_flow_sample: when `trace` is not NULL, thread 0 of
+ * every CTA writes two %globaltimer stamps (ns) per phase p:
+ * trace[(p * grid + cta) * 2 + 0] when the CTA finished phase p's work and
+ * trace[(p * grid + cta) * 2 + 1] when it left the barrier that follows.
+ * `trace` holds ee_flow_sample_phases() * grid * 2 entries (grid from
+ * ee_flow_sample_geometry). */
+int ee_flow_sample_traced(const ee_expert* ex, const void* x_in, const void* t0, void* x_out,
+                          int32_t n_steps, int32_t mode, void* workspace, size_t workspace_bytes,
+                          uint64_t* trace, ee_stream_t stream);
+/* Number of phases of one ee_flow_sample launch (0 for invalid arguments). */
+int32_t ee_flow_sample_phases(const ee_expert* ex, int32_t n_steps);
+
 /* Full validation of an expert description: every scalar field, and every
  * block record from a HOST copy of the table that ex->blocks points to on
  * the device. ee_flow_sample re-checks only the scalar fields (it never reads
@@ -160,6 +174,12 @@ int ee_flow_sample(const ee_expert* ex, const void* x_in, const void* t0, void* 
  * (timeout_ns, at most 2 s) and leaves EE_ERR_TIMEOUT in the status word of
  * `workspace` (>= 256 bytes, read it with ee_read_status). */
 int ee_barrier_selftest(void* workspace, uint64_t timeout_ns, ee_stream_t stream);
+
+/* Launch geometry ee_flow_sample uses for this expert on the current device:
+ * CTAs in the grid (one per SM at most), CTAs per cluster, dynamic shared
+ * memory per CTA. */
+int ee_flow_sample_geometry(const ee_expert* ex, int32_t* grid_ctas, int32_t* cluster,
+                            size_t* smem_bytes);
 
 /* Synchronises `stream` and copies the workspace status word to *status. */
 int ee_read_status(const void* workspace, int32_t* status, ee_stream_t stream);

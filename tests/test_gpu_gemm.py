@@ -192,10 +192,12 @@ def test_quant_linear_module(cuda):
     x = torch.randn(4, 50, 1024, device=cuda, dtype=torch.bfloat16)
     for bits in (8, 4):
         ql = TritonQuantLinear(lin, bits).to(cuda)
-        q, s, gs = quantize_weight(lin.weight.float().cpu(), bits, 128)
+        q, s, gs = quantize_weight(lin.weight.detach().float().cpu(), bits, 128)
         wd = (q.float() * s).reshape(768, 1024)
-        ref = torch.nn.functional.linear(x.float().cpu(), wd.bfloat16().float(), lin.bias.float().cpu())
-        y = ql(x)
+        ref = torch.nn.functional.linear(x.float().cpu(), wd.bfloat16().float(),
+                                         lin.bias.detach().float().cpu())
+        with torch.no_grad():
+            y = ql(x)
         assert y.shape == (4, 50, 768) and y.dtype == torch.bfloat16
         assert rel_err(y.float().cpu().numpy(), ref.numpy()) <= TOL
         assert ql.weight.dtype == (torch.uint8 if bits == 4 else torch.int8)
