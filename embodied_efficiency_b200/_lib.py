@@ -73,6 +73,8 @@ SIGNATURES = {
     "ee_flow_sample_geometry": (c_int32, [ctypes.POINTER(Expert), ctypes.POINTER(c_int32),
                                           ctypes.POINTER(c_int32), ctypes.POINTER(c_size_t)]),
     "ee_barrier_selftest": (c_int32, [c_void_p, ctypes.c_uint64, c_void_p]),
+    "ee_flow_sample_noalloc": (c_int32, [ctypes.POINTER(Expert), c_void_p, c_void_p, c_void_p, c_int32,
+                                         c_int32, c_void_p]),
 }
 
 _lib = None

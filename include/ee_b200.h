@@ -181,6 +181,31 @@ int ee_barrier_selftest(void* workspace, uint64_t timeout_ns, ee_stream_t stream
 int ee_flow_sample_geometry(const ee_expert* ex, int32_t* grid_ctas, int32_t* cluster,
                             size_t* smem_bytes);
 
+/*
+ * ee_flow_sample without a caller workspace, for callers that cannot allocate
+ * device memory: a hard-real-time control loop must not call cudaMalloc (it
+ * can synchronise the device and take an unbounded time mid-period), and a
+ * host binding this library through an FFI may own all device memory through
+ * its own allocator. No counterpart in the reference.
+ *   - The workspace is a fixed 4 MiB array in the library's device image
+ *     (held on every GPU that loads the library until the process exits);
+ *     calls whose ee_flow_sample_workspace_bytes() exceed it return
+ *     EE_ERR_WORKSPACE and launch nothing.
+ *   - Allocates nothing: no cudaMalloc / cudaFree, no allocating library call.
+ *   - The first call on a device looks up the array's device address; make
+ *     that first call before any stream capture on that device.
+ *   - All calls on a device share the one array, which keeps the last call's
+ *     contents; each call clears the parts that must start at zero (barrier
+ *     counter, status word, row statistics) before its launch. Calls that
+ *     overlap on the GPU (other streams, other threads) race on the array:
+ *     serialise them.
+ *   - Launch errors come back as return codes; the device-side status word
+ *     lives in the array, out of the caller's reach (use ee_flow_sample with
+ *     a workspace of your own where that word is needed).
+ */
+int ee_flow_sample_noalloc(const ee_expert* ex, const void* x_in, const void* t0, void* x_out,
+                           int32_t n_steps, int32_t mode, ee_stream_t stream);
+
 /* Synchronises `stream` and copies the workspace status word to *status. */
 int ee_read_status(const void* workspace, int32_t* status, ee_stream_t stream);
 
