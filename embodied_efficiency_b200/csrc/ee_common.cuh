@@ -100,6 +100,11 @@ EE_DEV float ld_act_f32(const float* p) {
   asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(r) : "l"(p) : "memory");
   return r;
 }
+EE_DEV float2 ld_act_f2(const float* p) {
+  float2 r;
+  asm volatile("ld.global.cg.v2.f32 {%0,%1}, [%2];" : "=f"(r.x), "=f"(r.y) : "l"(p) : "memory");
+  return r;
+}
 template <typename T> EE_DEV float ld_act_scalar(const T* p) {
   uint16_t b = ld_act2(p);
   return Act<T>::to_f(*reinterpret_cast<T*>(&b));
@@ -248,6 +253,9 @@ EE_DEV float4 ld_dsmem_f4(uint32_t addr) {
   asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
   return v;
+}
+EE_DEV void st_dsmem_f2(uint32_t addr, float a, float b) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
 }
 EE_DEV float ld_dsmem_f32(uint32_t addr) {
   float v;

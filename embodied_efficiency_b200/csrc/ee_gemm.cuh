@@ -46,8 +46,8 @@ struct GemmArgs {
   int has_bias;
   int split;           // CTAs of a cluster per unit (a power of two dividing the cluster)
   int lsplit;          // log2(split)
-  // Row statistics are kept as partial (sum, sum of squares) per 128-column
-  // tile of the row: [M][stat_slots][2], summed in slot order (deterministic).
+  // Row statistics are kept as partial (sum, sum of squares) per 16-column
+  // slice of the row: [M][stat_slots][2], summed in slot order (deterministic).
   int stat_slots;
   // input normalisation: when in_stats is set, every staged activation row is
   // normalised with its statistics over K and the weight / bias in_w / in_b
@@ -57,17 +57,19 @@ struct GemmArgs {
   const void* in_b;
   int in_norm;            // EE_NORM_*
   float in_eps;
-  // output statistics: when out_stats is set, each unit writes the (sum, sum
-  // of squares) of its 128 output columns of every token row to slot n-tile
+  // output statistics: when out_stats is set, each CTA writes the (sum, sum
+  // of squares) of its output columns of every token row to the slot of its
+  // first 16 columns, and zeros to the slots of its other 16-column slices
   float* out_stats;       // [M][stat_slots][2]
 };
 
 // Shared memory of a GEMM unit (byte offsets from the dynamic base).
 //   x    activation slice [64 tok][KS] (16-byte chunks swizzled, see
 //        x_chunk); after the MMAs it holds the reduced tile E[64][128/S]
-//   p    this CTA's partial tile [128 rows][kPS] fp32
-//   aux  norm weight/bias slice, row statistics, bias, output-stat partials
-//        and the residual tile of the unit
+//   p    two receive buffers (alternating by round) for the partial tiles the
+//        sub-cluster's CTAs push here: [S][128/S rows][kPS] fp32 each
+//   aux  norm weight/bias slice, row statistics, bias, staged scales and the
+//        residual tile of the unit
 //   pre  weight words of the first unit, copied in before a grid barrier
 struct GemmSmem {
   uint32_t x, p, aux, pre;
@@ -76,8 +78,7 @@ struct GemmSmem {
 constexpr uint32_t kAuxGB = 0;                 // [2][2048] act: norm weight, bias slice
 constexpr uint32_t kAuxRow = 8192;             // [64][2] float: mean, rstd
 constexpr uint32_t kAuxBias = kAuxRow + 512;   // [128] float
-constexpr uint32_t kAuxOst = kAuxBias + 512;   // [64][2] float: output-stat partials
-constexpr uint32_t kAuxRes = kAuxOst + 512;    // [64][128] act: residual tile
+constexpr uint32_t kAuxRes = kAuxBias + 512;   // [64][128] act: residual tile
 constexpr uint32_t kAuxScale = kAuxRes + 64 * 128 * 2;  // [kMaxKB][2][8 warps][8 g] float
 constexpr int kMaxKB = 16;                     // k-blocks per CTA with staged scales
 constexpr uint32_t kAuxBytes = kAuxScale + kMaxKB * 2 * 64 * 4;
@@ -230,7 +231,7 @@ struct Gemm {
   // One unit: rows nt*128 .. +127 x tokens m0 .. m0+63 over all of K, by the S
   // CTAs of sub-cluster rank/S. Every CTA of the cluster calls this the same
   // number of times (inactive CTAs only join the cluster barriers).
-  static EE_DEV void unit(const GemmArgs& a, bool active, int nt, int m0, char* smem,
+  static EE_DEV void unit(const GemmArgs& a, bool active, int nt, int m0, int parity, char* smem,
                           const GemmSmem& sm, const PreRegs* pre) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const ee_linear& L = a.w;
@@ -247,7 +248,6 @@ struct Gemm {
     char* aux = smem + sm.aux;
     float* rowst = reinterpret_cast<float*>(aux + kAuxRow);
     float* sbias = reinterpret_cast<float*>(aux + kAuxBias);
-    float* ost = reinterpret_cast<float*>(aux + kAuxOst);
     T* sres = reinterpret_cast<T*>(aux + kAuxRes);
 
     float acc[8][4];
@@ -316,24 +316,42 @@ struct Gemm {
         const int n = nbase + threadIdx.x;
         sbias[threadIdx.x] = (a.has_bias && n < L.n) ? ld_param(reinterpret_cast<const T*>(L.bias) + n) : 0.f;
       }
-      if (a.in_stats && threadIdx.x < mrows) {
-        const float* sp = a.in_stats + 2 * (size_t)(m0 + threadIdx.x) * a.stat_slots;
-        float2 st = make_float2(0.f, 0.f);
-        for (int q = 0; q < a.stat_slots; ++q) {  // fixed order: deterministic
-          st.x += ld_act_f32(sp + 2 * q);
-          st.y += ld_act_f32(sp + 2 * q + 1);
+      if (a.in_stats) {
+        // 4 threads per token row, each summing every 4th slot in order; the
+        // four partials are combined in a fixed tree order (deterministic)
+        const int tok = threadIdx.x >> 2, part = threadIdx.x & 3;
+        float sx = 0.f, sxx = 0.f;
+        if (tok < mrows) {
+          const float* sp = a.in_stats + 2 * (size_t)(m0 + tok) * a.stat_slots;
+          float2 v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int q = part + 4 * i;
+            v[i] = q < a.stat_slots ? ld_act_f2(sp + 2 * q) : make_float2(0.f, 0.f);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            sx += v[i].x;
+            sxx += v[i].y;
+          }
         }
-        const float inv_k = 1.0f / (float)L.k;
-        float mean = 0.f, rstd;
-        if (a.in_norm == EE_NORM_RMS) {
-          rstd = 1.0f / sqrtf(st.y * inv_k + a.in_eps);
-        } else {
-          mean = st.x * inv_k;
-          const float var = fmaxf(st.y * inv_k - mean * mean, 0.f);
-          rstd = 1.0f / sqrtf(var + a.in_eps);
+        sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+        sxx += __shfl_xor_sync(0xffffffffu, sxx, 1);
+        sx += __shfl_xor_sync(0xffffffffu, sx, 2);
+        sxx += __shfl_xor_sync(0xffffffffu, sxx, 2);
+        if (part == 0 && tok < mrows) {
+          const float inv_k = 1.0f / (float)L.k;
+          float mean = 0.f, rstd;
+          if (a.in_norm == EE_NORM_RMS) {
+            rstd = 1.0f / sqrtf(sxx * inv_k + a.in_eps);
+          } else {
+            mean = sx * inv_k;
+            const float var = fmaxf(sxx * inv_k - mean * mean, 0.f);
+            rstd = 1.0f / sqrtf(var + a.in_eps);
+          }
+          rowst[2 * tok] = mean;
+          rowst[2 * tok + 1] = rstd;
         }
-        rowst[2 * threadIdx.x] = mean;
-        rowst[2 * threadIdx.x + 1] = rstd;
       }
     }
     // 2. weights of the first k-block (from the pre area, or loaded now)
@@ -443,29 +461,34 @@ struct Gemm {
         }
       }
 
-      // 5. partial tile -> P
-      float* P = reinterpret_cast<float*>(smem + sm.p);
+      // 5. push the partial tile: rows of rank q go to rank q's receive buffer
+      const uint32_t rbuf = sbase + sm.p + (uint32_t)(parity * kPBytes);
+      const int rshift = 7 - a.lsplit;  // log2(RPR)
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         if (j < JT) {
-          const int r0 = 16 * warp + g, c0 = 8 * j + 2 * t;
-          *reinterpret_cast<float2*>(P + r0 * kPS + c0) = make_float2(acc[j][0], acc[j][1]);
-          *reinterpret_cast<float2*>(P + (r0 + 8) * kPS + c0) = make_float2(acc[j][2], acc[j][3]);
+          const int c0 = 8 * j + 2 * t;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int row = 16 * warp + g + 8 * h;
+            const int owner = row >> rshift, lrow = row & (RPR - 1);
+            const uint32_t off = (uint32_t)(((r * RPR + lrow) * kPS + c0) * 4);
+            st_dsmem_f2(mapa(rbuf + off, (uint32_t)(sub0 + owner)), acc[j][2 * h], acc[j][2 * h + 1]);
+          }
         }
     }
-    cluster_sync();
+    cluster_sync();  // every partial of this round has arrived
 
-    // 6. reduce this CTA's RPR rows over the S partial tiles of the sub-cluster
+    // 6. sum the S partials of this CTA's RPR rows (local, source order)
     float* E = reinterpret_cast<float*>(smem + sm.x);  // [64][RPR], reuses the X slice
     if (active) {
-      const uint32_t pbase = sbase + sm.p;
+      const float* R = reinterpret_cast<const float*>(smem + sm.p + parity * kPBytes);
       for (int i = threadIdx.x; i < RPR * 16; i += kThreads) {
         const int row = i >> 4, c4 = i & 15;
         if (4 * c4 < JT * 8) {
-          const uint32_t off = (uint32_t)(((r * RPR + row) * kPS + 4 * c4) * 4);
           float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
           for (int q = 0; q < S; ++q) {
-            const float4 v = ld_dsmem_f4(mapa(pbase + off, (uint32_t)(sub0 + q)));
+            const float4 v = *reinterpret_cast<const float4*>(R + (q * RPR + row) * kPS + 4 * c4);
             sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
           }
           E[(4 * c4 + 0) * RPR + row] = sum.x;
@@ -509,34 +532,25 @@ struct Gemm {
             if (n0 + e < L.n) dst[e] = Act<T>::from_f(v[e]);
         }
       }
+      // 8. row statistics of this CTA's columns (column order), one slot each
       if (a.out_stats) {
         __syncthreads();
-        if (threadIdx.x < mrows) {  // this CTA's columns of one row, in column order
+        if (threadIdx.x < mrows) {
           float sx = 0.f, sxx = 0.f;
           for (int col = 0; col < RPR; ++col) {
             const float y = E[threadIdx.x * RPR + col];
             sx += y;
             sxx += y * y;
           }
-          ost[2 * threadIdx.x] = sx;
-          ost[2 * threadIdx.x + 1] = sxx;
+          float* st = a.out_stats + 2 * ((size_t)(m0 + threadIdx.x) * a.stat_slots + (nbase >> 4));
+          st[0] = sx;
+          st[1] = sxx;
+          for (int q = 1; q < (RPR >> 4); ++q) {
+            st[2 * q] = 0.f;
+            st[2 * q + 1] = 0.f;
+          }
         }
       }
-    }
-    cluster_sync();  // peers are done with this CTA's P; the partial stats are complete
-
-    // 8. the sub-cluster's first CTA combines the row statistics of its unit
-    if (active && a.out_stats && r == 0 && threadIdx.x < mrows) {
-      const uint32_t obase = sbase + sm.aux + kAuxOst + threadIdx.x * 8;
-      float sx = 0.f, sxx = 0.f;
-      for (int q = 0; q < S; ++q) {  // rank order: deterministic
-        const uint32_t ad = mapa(obase, (uint32_t)(sub0 + q));
-        sx += ld_dsmem_f32(ad);
-        sxx += ld_dsmem_f32(ad + 4);
-      }
-      float* st = a.out_stats + 2 * ((size_t)(m0 + threadIdx.x) * a.stat_slots + nt);
-      st[0] = sx;
-      st[1] = sxx;
     }
     __syncthreads();  // shared memory reuse by the next unit
   }
@@ -544,6 +558,7 @@ struct Gemm {
   // All units of a GEMM in rounds over the cluster slots; `pre` applies to
   // this CTA's first unit.
   static EE_DEV void run(const GemmArgs& a, char* smem, const GemmSmem& sm, const PreRegs* pre) {
+    if ((int)cl_size() < a.split) return;  // launched without the planned cluster: no work
     const int n_tiles = (a.w.n + kRU - 1) / kRU;
     const int units = n_tiles * ((a.M + kMTile - 1) / kMTile);
     const int per_cluster = (int)cl_size() >> a.lsplit;
@@ -553,12 +568,13 @@ struct Gemm {
     for (int rd = 0; rd < rounds; ++rd) {
       const int u = rd * slots + slot;
       const bool act = u < units;
-      unit(a, act, act ? u % n_tiles : 0, act ? (u / n_tiles) * kMTile : 0, smem, sm,
+      unit(a, act, act ? u % n_tiles : 0, act ? (u / n_tiles) * kMTile : 0, rd & 1, smem, sm,
            (rd == 0 && act) ? pre : nullptr);
     }
   }
   // Start the prefetch of this CTA's first unit; returns whether it has one.
   static EE_DEV bool start_prefetch(const GemmArgs& a, const GemmSmem& sm, char* smem, PreRegs& pr) {
+    if ((int)cl_size() < a.split) return false;
     const int n_tiles = (a.w.n + kRU - 1) / kRU;
     const int units = n_tiles * ((a.M + kMTile - 1) / kMTile);
     const int per_cluster = (int)cl_size() >> a.lsplit;

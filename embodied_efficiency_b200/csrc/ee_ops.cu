@@ -65,14 +65,16 @@ static int launch_gemm_k(GemmArgs a, cudaStream_t s) {
   GemmSmem sm;
   sm.x = 0;
   sm.p = (uint32_t)x;
-  sm.aux = (uint32_t)(x + kPBytes);
+  sm.aux = (uint32_t)(x + 2 * kPBytes);
   sm.pre = (uint32_t)(sm.aux + kAuxBytes);
-  // stage the unit's weights with cp.async (up to 64 KB of k-blocks)
-  const size_t kbs = (size_t)(a.w.k / cl / kKBlock) * pre_kb_bytes(KIND);
-  sm.pre_bytes = (uint32_t)(kbs < 65536 ? kbs : (65536 / pre_kb_bytes(KIND)) * pre_kb_bytes(KIND));
-  const size_t smem = sm.pre + sm.pre_bytes;
   const DevProps* dp = device_props();
-  if (!dp || smem + 1024 > (size_t)dp->smem_optin) return EE_ERR_UNSUPPORTED;
+  if (!dp || (size_t)sm.pre + 1024 > (size_t)dp->smem_optin) return EE_ERR_UNSUPPORTED;
+  // stage the unit's weights with cp.async: as many whole k-blocks as fit (at most 64 KB)
+  size_t room = (size_t)dp->smem_optin - 1024 - sm.pre;
+  if (room > 65536) room = 65536;
+  const size_t kbs = (size_t)(a.w.k / cl / kKBlock) * pre_kb_bytes(KIND);
+  sm.pre_bytes = (uint32_t)(kbs < room ? kbs : (room / pre_kb_bytes(KIND)) * pre_kb_bytes(KIND));
+  const size_t smem = sm.pre + sm.pre_bytes;
   auto fn = wq_gemm_kernel<T, KIND>;
   static std::atomic<int> smem_set[64];
   allow_max_smem(fn, smem_set);

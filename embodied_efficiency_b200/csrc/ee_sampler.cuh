@@ -44,12 +44,15 @@ struct Ctx {
   unsigned* bar;
   int* abort_flag;
   int* status;
-  float* stats;  // [2 step parities][n_inst][M][n_slots][2] row (sum, sum of squares)
+  float* stats;  // [2][M][n_slots][2] row (sum, sum of squares) of the norm inputs,
+                 // alternating between the two halves by norm sequence number
   int n_inst;    // norms per step (3 per block, 2 without self-attention)
-  int n_slots;   // partial-statistics slots per row: 128-column tiles of d
+  int n_slots;   // partial-statistics slots per row: 16-column slices of d
   uint32_t desc; // shared-memory copy of the block table (byte offset)
   int ks_cap;    // largest K slice a GEMM unit may stage
   int lsplit[7]; // log2 CTAs per unit of t_proj, qkv, proj, q_c, out_c, mlp0, mlp2
+  int cluster;   // cluster size and grid the splits were planned for
+  int grid;
   void *x, *qkv, *att, *qb, *hid, *emb, *temb;
   GemmSmem sm;
   size_t smem_bytes;
@@ -90,7 +93,7 @@ EE_DEV int inst_first(const Ctx& c, int l) { return l * (c.ex.self_attn ? 3 : 2)
 EE_DEV int inst_x(const Ctx& c, int l) { return c.ex.self_attn ? 3 * l + 1 : 2 * l; }
 EE_DEV int inst_2(const Ctx& c, int l) { return c.ex.self_attn ? 3 * l + 2 : 2 * l + 1; }
 EE_DEV float* stats_of(const Ctx& c, int step, int inst) {
-  return c.stats + ((size_t)((step & 1) * c.n_inst + inst) * c.M) * c.n_slots * 2;
+  return c.stats + (size_t)((step * c.n_inst + inst) & 1) * c.M * c.n_slots * 2;
 }
 
 EE_DEV GemmArgs make_gemm(const Ctx& c, const Phase& ph, const char* smem) {
@@ -315,10 +318,11 @@ EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head,
   }
   s = block_sum(s, red);
   ss = block_sum(ss, red);
-  if (tid == 0) {  // slot 0 holds the whole row (the other slots stay zero)
-    float* st = stats_of(c, head_step, 0) + 2 * (size_t)m * c.n_slots;
-    st[0] = s;
-    st[1] = ss;
+  // slot 0 holds the whole row, the other slots are zero
+  float* st = stats_of(c, head_step, 0) + 2 * (size_t)m * c.n_slots;
+  if (tid < c.n_slots) {
+    st[2 * tid] = tid == 0 ? s : 0.f;
+    st[2 * tid + 1] = tid == 0 ? ss : 0.f;
   }
 }
 
@@ -369,6 +373,12 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
   const int P = num_phases(c);
   const int d = c.ex.d_model;
   unsigned target = 0;
+  // The work split was planned for this launch shape; any other shape (a
+  // launch path that dropped the cluster dimension, say) does no work.
+  if ((int)cl_size() != c.cluster || (int)gridDim.x != c.grid) {
+    if (threadIdx.x == 0) atomicCAS(c.status, 0, (int)EE_ERR_LAUNCH);
+    return;
+  }
   {  // block table -> shared memory (read by every GEMM phase)
     const unsigned long long* src = reinterpret_cast<const unsigned long long*>(c.ex.blocks);
     unsigned long long* dst = reinterpret_cast<unsigned long long*>(smem + c.desc);
@@ -379,14 +389,6 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
 
   for (int p = 0; p < P; ++p) {
     const Phase ph = decode(c, p);
-    // the first block phase of step k clears the statistics step k+1 uses
-    if ((ph.type == PH_GEMM || ph.type == PH_ATTN_SELF || ph.type == PH_ATTN_CROSS) &&
-        ph.layer == 0 && ph.sub == (c.ex.self_attn ? 0 : 3)) {
-      float* st = c.stats + (size_t)(((ph.step + 1) & 1) * c.n_inst) * c.M * c.n_slots * 2;
-      const size_t n = (size_t)c.n_inst * c.M * c.n_slots * 2;
-      for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += (size_t)gridDim.x * kThreads)
-        st[i] = 0.f;
-    }
     switch (ph.type) {
       case PH_EMB: {
         const int half = d / 2;
@@ -489,8 +491,8 @@ inline Layout layout_for(const ee_expert& ex, int n_steps) {
   L.Rt_max = n_steps * ex.batch;
   size_t off = 0;
   L.sync = off; off += 256;
-  L.n_slots = (ex.d_model + kRU - 1) / kRU;
-  L.stats = off; off += al256((size_t)2 * L.n_inst * L.M * L.n_slots * 2 * sizeof(float));
+  L.n_slots = (ex.d_model + 15) / 16;
+  L.stats = off; off += al256((size_t)2 * L.M * L.n_slots * 2 * sizeof(float));
   L.x = off; off += al256((size_t)L.M * d * e);
   L.qkv = off; off += ex.self_attn ? al256((size_t)L.M * 3 * d * e) : 0;
   L.att = off; off += al256((size_t)L.M * d * e);
@@ -534,7 +536,7 @@ inline SamplerSmem sampler_smem_map(const ee_expert& ex, int smem_optin) {
   SamplerSmem sm;
   sm.g.x = 0;
   sm.g.p = (uint32_t)x;
-  sm.g.aux = (uint32_t)(x + kPBytes);
+  sm.g.aux = (uint32_t)(x + 2 * kPBytes);
   // the block table must survive the attention phases, which use [0, attn)
   const size_t hd = ex.n_heads > 0 ? ex.d_model / ex.n_heads : 64;
   const size_t attn = hd == 128 ? AttnSmem<128>::kTotal : AttnSmem<64>::kTotal;
@@ -683,6 +685,8 @@ int launch_sampler(Ctx c, cudaStream_t s) {
   if (rc) return rc;
   rc = plan_splits(c, grid, cl);
   if (rc) return rc;
+  c.cluster = cl;
+  c.grid = grid;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
