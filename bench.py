@@ -176,14 +176,15 @@ def gemm_sweep(device, flush):
         q, s, gs = quantize_weight(w, bits, 128)
         q2 = q.reshape(n, k).to(device)
         mats[bits] = (_pack_int4(q2) if bits == 4 else q2, s.reshape(n, -1).to(device))
-    for m in (1, 16, 50):
+    for m in (1, 16, 50, 128, 512):
         x = torch.randn(m, k, generator=g).bfloat16().to(device)
         for bits, (wt, sc) in mats.items():
             ms = time_calls(lambda: wq_linear(x, wt, sc, None, 128, bits), 50, 5, flush)
             t = statistics.median(ms)
             nbytes = linear_bytes(n, k, bits) - n * 2 + m * k * 2 + m * n * 2
             out[f"m{m}_{'bf16' if bits == 16 else f'int{bits}'}"] = {
-                "us": round(t * 1e3, 2), "GBps": round(nbytes / (t * 1e-3) / 1e9, 1)}
+                "us": round(t * 1e3, 2), "GBps": round(nbytes / (t * 1e-3) / 1e9, 1),
+                "TFLOPs": round(2.0 * m * n * k / (t * 1e-3) / 1e12, 1)}
     return out
 
 
@@ -248,6 +249,50 @@ def run_reference(args):
     print(json.dumps(line))
 
 
+def profile_case(spec, launches):
+    """A few launches of one kernel for a profiler (no timing, no JSON):
+    ``gemm:M:K:BITS`` runs the standalone dequant-GEMM on a square K=N weight,
+    ``sampler:BITS`` replays the captured sampler call (a plain cluster launch
+    inside a CUDA graph)."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    kind, *rest = spec.split(":")
+    if kind == "gemm":
+        from embodied_efficiency_b200 import wq_linear
+        from embodied_efficiency_b200.quant import quantize_weight
+        from embodied_efficiency_b200.wq_gemm import _pack_int4
+        m, k, bits = (int(v) for v in rest)
+        g = torch.Generator(device="cpu").manual_seed(0)
+        w = torch.randn(k, k, generator=g) * 0.02
+        if bits == 16:
+            wt, sc = w.bfloat16().to(dev), None
+        else:
+            q, s, _ = quantize_weight(w, bits, 128)
+            q2 = q.reshape(k, k).to(dev)
+            wt, sc = (_pack_int4(q2) if bits == 4 else q2), s.reshape(k, -1).to(dev)
+        x = torch.randn(m, k, generator=g).bfloat16().to(dev)
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        for _ in range(launches):
+            flush.zero_()
+            y = wq_linear(x, wt, sc, None, 128, bits)
+        torch.cuda.synchronize()
+        print(f"gemm m={m} k=n={k} bits={bits} mean|y|={float(y.float().abs().mean()):.5f}")
+    elif kind == "sampler":
+        from embodied_efficiency_b200 import GraphedSampler
+        bits = int(rest[0]) if rest else 4
+        m, x0, prefix = build_expert(bits, dev)
+        x = x0.to(dev).bfloat16()
+        gs = GraphedSampler(m, x, N_STEPS, warmup=1)
+        for _ in range(launches):
+            y = gs.run(x)
+        torch.cuda.synchronize()
+        if gs.status() != 0:
+            raise RuntimeError(f"sampler status {gs.status()}")
+        print(f"sampler bits={bits} mean|x|={float(y.float().abs().mean()):.5f}")
+    else:
+        raise SystemExit(f"unknown --profile case {spec!r}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -256,8 +301,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--profile", default=None,
+                    help="gemm:M:K:BITS or sampler:BITS -- a few launches for a profiler")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.profile:
+        return profile_case(args.profile, max(args.steps if args.steps != 200 else 4, 1))
     if args.impl == "reference":
         return run_reference(args)
 

@@ -1,5 +1,6 @@
 // ee_ops.cu -- C ABI: int4 pack / unpack and the standalone dequant-GEMM.
 #include <atomic>
+#include <mutex>
 
 #include "ee_gemm.cuh"
 #include "ee_host.h"
@@ -97,8 +98,43 @@ static int launch_gemm_k(GemmArgs a, cudaStream_t s) {
   return err == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
 }
 
+// Streaming small-M path (ee_stream.cuh, instantiated in ee_stream_*.cu) and
+// the tensor-core path (ee_tc.cuh, instantiated in ee_tc_*.cu).
+template <typename T> int launch_stream(const GemmArgs& g, int* status, cudaStream_t st, bool* used);
+template <typename T> int launch_tc(const GemmArgs& g, int* status, cudaStream_t st, bool* used);
+
+// Token count up to which the warp-MMA streaming kernel is used; above it
+// the tcgen05 kernel.
+constexpr int kStreamMaxM = 16;
+
+// Status word of the GEMM kernels (first error since the last reset).
+static __device__ int g_gemm_status;
+
+static int* gemm_status_ptr() {
+  static std::mutex mu;
+  static int* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> g(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_gemm_status) != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<int*>(p);
+  }
+  return addr[dev];
+}
+
 template <typename T>
 int launch_gemm_d(const GemmArgs& a, cudaStream_t s) {
+  bool used = false;
+  int* status = gemm_status_ptr();
+  int rc = EE_OK;
+  if (a.M <= kStreamMaxM) {
+    rc = launch_stream<T>(a, status, s, &used);
+    if (used || rc != EE_OK) return rc;
+  }
+  rc = launch_tc<T>(a, status, s, &used);
+  if (used || rc != EE_OK) return rc;
   switch (a.w.wkind) {
     case EE_W_DENSE: return launch_gemm_k<T, EE_W_DENSE>(a, s);
     case EE_W_INT8: return launch_gemm_k<T, EE_W_INT8>(a, s);
@@ -181,6 +217,21 @@ int ee_wq_gemm(const void* x, const void* weight, const void* scales, const void
   a.has_bias = (epilogue & EE_EPI_BIAS) ? 1 : 0;
   cudaStream_t s = (cudaStream_t)stream;
   return act_dtype == EE_BF16 ? launch_gemm_d<__nv_bfloat16>(a, s) : launch_gemm_d<__half>(a, s);
+}
+
+int ee_wq_gemm_status(int32_t* status, int32_t reset) {
+  if (!status) return EE_ERR_ARG;
+  int rc = check_device();
+  if (rc) return rc;
+  if (cudaDeviceSynchronize() != cudaSuccess) return EE_ERR_LAUNCH;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(int)) != cudaSuccess) return EE_ERR_LAUNCH;
+  *status = v;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(int)) != cudaSuccess) return EE_ERR_LAUNCH;
+  }
+  return EE_OK;
 }
 
 }  // extern "C"

@@ -1,0 +1,99 @@
+// ee_umma.cuh -- 5th-generation tensor-core (tcgen05) primitives for sm_100a:
+// tensor-memory (TMEM) allocation, the single-thread-issued MMA with its
+// shared-memory operand descriptors, completion tracking through mbarriers,
+// and TMEM -> register loads for the epilogue.
+//
+// Operand layout used throughout: K-major tiles of 16-bit elements written
+// with the 128-byte swizzle (a row of 64 k = 128 bytes per shared-memory line,
+// eight lines per 1024-byte swizzle atom, 16-byte chunk index XORed with the
+// line index modulo 8) -- the layout TMA produces with
+// CU_TENSOR_MAP_SWIZZLE_128B and the one the dequantising warps write by hand.
+#pragma once
+
+#include "ee_common.cuh"
+
+namespace ee {
+
+// ---- TMEM allocation (one full warp executes these) -----------------------
+EE_DEV void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+EE_DEV void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+EE_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// ---- ordering of tcgen05 operations around thread synchronisation --------
+EE_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+EE_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// generic-proxy shared-memory writes -> visible to the async proxy (MMA reads)
+EE_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---- descriptors ------------------------------------------------------------
+// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile whose
+// first row starts at `saddr` (inside a 1024-byte aligned swizzle atom):
+// start address >> 4 in bits [0,14), leading byte offset 1 (unused for this
+// layout), stride byte offset 1024 >> 4 = 64 (between 8-row groups) in bits
+// [32,46), descriptor version 1 in bits [46,48), layout type 2 (128-byte
+// swizzle) in bits [61,64).
+EE_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)64u << 32) |
+         ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+
+// Instruction descriptor of kind::f16 with fp32 accumulation, both operands
+// K-major: D format f32 (bit 4), A / B format (bits 7 and 10: 0 = f16,
+// 1 = bf16), N >> 3 in bits [17,23), M >> 4 in bits [24,29).
+template <typename T> __host__ __device__ constexpr uint32_t umma_idesc(int m, int n);
+template <> __host__ __device__ constexpr uint32_t umma_idesc<__nv_bfloat16>(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+template <> __host__ __device__ constexpr uint32_t umma_idesc<__half>(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// ---- MMA: D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread -----------
+EE_DEV void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on `bar` when every tcgen05 operation this thread issued so far
+// has completed.
+EE_DEV void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// ---- TMEM -> registers: 32 lanes x 16 consecutive 32-bit columns ----------
+// A warp may only touch the 32-lane quarter (warp id % 4) of TMEM.
+EE_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+EE_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// packed multiply in the activation type
+template <typename T> EE_DEV uint32_t hmul2(uint32_t a, uint32_t b);
+template <> EE_DEV uint32_t hmul2<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+template <> EE_DEV uint32_t hmul2<__half>(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+}  // namespace ee

@@ -7,6 +7,8 @@ Layouts are the reference's: int8 weights [N, K]; int4 packed two per byte
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
@@ -104,6 +106,15 @@ def wq_linear(x, weight, scales, bias, group_size, bits, zeros=None, gelu=False,
         _lib.scale_code(s.dtype) if s is not None else _lib.EE_F32, epi, _lib.stream_ptr(x.device))
     _lib.check(rc, "ee_wq_gemm")
     return y.reshape(*lead, n).to(out_dtype)
+
+
+def gemm_status(reset: bool = False) -> int:
+    """Device status word of the dequant-GEMM kernels on the current device
+    (0, or the first error a launch recorded: a bounded in-kernel wait that
+    gave up, or a launch without its planned cluster shape). Synchronises."""
+    st = ctypes.c_int32(0)
+    _lib.check(_lib.load().ee_wq_gemm_status(ctypes.byref(st), 1 if reset else 0), "ee_wq_gemm_status")
+    return int(st.value)
 
 
 class TritonQuantLinear(nn.Module):

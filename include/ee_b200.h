@@ -13,6 +13,7 @@
  *   ee_unpack_int4        kernel/triton_gemm.py:42-48   _unpack_int4
  *   ee_wq_gemm            kernel/triton_gemm.py:141-164 wq_linear
  *                         (+ the Triton kernels at :75-138 it launches)
+ *   ee_wq_gemm_status     device status word of the dequant-GEMM (new)
  *   ee_flow_sample        kernel/flow_expert.py:127-137 flow_sample, run as
  *                         one fused launch over kernel/flow_expert.py:117-124
  *                         ActionExpert.forward and :83-95 Block.forward
@@ -102,6 +103,13 @@ int ee_wq_gemm(const void* x, const void* weight, const void* scales, const void
                const void* bias, const void* residual, void* y,
                int64_t m, int64_t n, int64_t k, int32_t wkind, int32_t group,
                int32_t act_dtype, int32_t scale_dtype, int32_t epilogue, ee_stream_t stream);
+
+/* Status word of the dequant-GEMM kernels on the current device: 0, or the
+ * first error a launch recorded since the last reset (EE_ERR_TIMEOUT: a
+ * bounded wait of the TMA pipeline gave up; EE_ERR_LAUNCH: a kernel found
+ * itself launched without its planned cluster shape and did no work).
+ * Synchronises the device; reset != 0 clears the word afterwards. (new) */
+int ee_wq_gemm_status(int32_t* status, int32_t reset);
 
 /* ---- fused flow-matching sampler --------------------------------------- */
 typedef struct ee_linear {

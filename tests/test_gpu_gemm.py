@@ -202,3 +202,10 @@ def test_quant_linear_module(cuda):
         assert rel_err(y.float().cpu().numpy(), ref.numpy()) <= TOL
         assert ql.weight.dtype == (torch.uint8 if bits == 4 else torch.int8)
         assert ql.scales.dtype == torch.float32 and ql.scales.shape == (768, 8)
+
+
+def test_zz_gemm_status_clean(cuda):
+    """No launch of this module's tests recorded an in-kernel timeout or a
+    launch-shape error."""
+    from embodied_efficiency_b200.wq_gemm import gemm_status
+    assert gemm_status(reset=True) == 0
