@@ -188,6 +188,35 @@ def gemm_sweep(device, flush):
     return out
 
 
+def fleet_run(expert, rank, world, dev, n_requests=256, chunk=32, steps=5, warmup=3):
+    """Fleet mode: n_requests independent int4 sampler requests (request r
+    seeded with r) sharded in contiguous blocks over the ranks, no collective;
+    device time of one fleet step (every chunk of this rank), max over ranks."""
+    from embodied_efficiency_b200 import synth
+    from embodied_efficiency_b200.fleet import FleetSampler
+    cfg = expert.cfg
+    fs = FleetSampler(n_requests, rank, world, chunk=chunk, expert=expert, device=dev)
+    fs.stage(lambda i: synth.fleet_request(cfg, i))
+    for _ in range(warmup):
+        fs.run_device()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fs.run_device()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = t.item()
+    return {"metric": "actions/s", "value": round(n_requests * cfg.horizon / (ms * 1e-3), 1),
+            "unit": "actions/s", "requests": n_requests, "requests_per_gpu": fs.hi - fs.lo,
+            "chunk": chunk, "ms_per_fleet_step": round(ms, 3), "n_gpus": world,
+            "workload": "256 requests x (10-step int4 group-128 sampler, d1024 L4, own prefix and noise)",
+            "scaling": "strong (fixed 256 requests split over the GPUs)", "collectives": "none on the data path"}
+
+
 def cpu_baseline_run(budget_s=15.0, bits=4):
     """The oracle (CPU restatement of the reference path) on the host cores."""
     from embodied_efficiency_b200 import synth
@@ -301,6 +330,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-fleet", action="store_true")
+    ap.add_argument("--fleet-chunk", type=int, default=32)
     ap.add_argument("--profile", default=None,
                     help="gemm:M:K:BITS or sampler:BITS -- a few launches for a profiler")
     args = ap.parse_args()
@@ -360,6 +391,8 @@ def main():
         torch.distributed.all_reduce(e2e_total, op=torch.distributed.ReduceOp.MAX)
     e2e_value = e2e_total.item() / (args.steps * world)
 
+    fleet = None if args.no_fleet else fleet_run(m, rank, world, dev, chunk=args.fleet_chunk)
+
     if rank != 0:
         if world > 1:
             torch.distributed.barrier()
@@ -400,6 +433,8 @@ def main():
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
+    if fleet is not None:
+        line["fleet"] = fleet
     if not args.no_sweep:
         line["gemm_k4096"] = gemm_sweep(dev, flush)
     if not args.no_cpu_baseline:

@@ -15,9 +15,10 @@
 //    stage guarded by a "full" mbarrier (TMA transaction bytes) and an
 //    "empty" mbarrier (the consuming warps), so up to nst k-blocks are in
 //    flight per SM;
-//  * eight consumer warps: warp = (row group rw: 32 rows, k group kg), the
-//    two k groups taking alternate k-blocks. Each warp dequantises its 32
-//    rows in registers (nibble / byte -> exact bf16/f16 integers, see
+//  * sixteen consumer warps: warp = (row group rw: 16 rows, k group kg), the
+//    two k groups taking alternate k-blocks (four warps per scheduler, so
+//    one warp's dependency stalls are covered by the others). Each warp
+//    dequantises its 16 rows in registers (nibble / byte -> exact bf16/f16 integers, see
 //    ee_gemm.cuh) and runs m16n8k16 MMAs with the weights as the A operand
 //    and the tokens as B; the fp32 per-(row, group) scale multiplies each
 //    k-block's partial sum;
@@ -40,7 +41,9 @@
 
 namespace ee {
 
-constexpr int kStreamWarps = 9;  // 8 consumer warps + 1 producer warp
+constexpr int kStreamCWarps = 16;  // consumer warps: 8 row groups x 2 k groups
+constexpr int kStreamCThreads = kStreamCWarps * 32;
+constexpr int kStreamWarps = kStreamCWarps + 1;  // + 1 producer warp
 constexpr int kStreamThreads = kStreamWarps * 32;
 constexpr int kStreamMaxTokens = 64;
 
@@ -59,6 +62,13 @@ struct StreamArgs {
   int ps;              // floats per row of a partial tile (8*JT + 4)
   uint32_t stage_bytes;
   uint32_t off_bar, off_scal, off_recv, off_res, off_bias;  // from the 1024-aligned base
+  // activations resident for the CTA's whole K slice (few tokens): copied
+  // once at the start into [kbc][2 boxes][8*JT rows][128 B] (128-byte
+  // swizzle), so the ring carries weights only
+  int xres;
+  uint32_t off_x;
+  const void* x;
+  long long ldx;
   int* status;         // device status word (EE_ERR_TIMEOUT / EE_ERR_LAUNCH)
   unsigned long long timeout_ns;
 };
@@ -92,18 +102,23 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const ee_linear& L = a.w;
   const uint32_t bar_full = sb + a.off_bar, bar_empty = bar_full + 8u * a.nst;
 
-  if (warp == 8 && lane == 0) {
+  if (warp == kStreamCWarps && lane == 0) {
     tma_prefetch_map(&tw);
-    tma_prefetch_map(&tx);
+    if (!a.xres) tma_prefetch_map(&tx);
+    for (int s = 0; s < a.nst; ++s) {
+      mbar_init(bar_full + 8u * s, 1);
+      mbar_init(bar_empty + 8u * s, kStreamCWarps / 2);
+    }
+    mbar_fence_init();
   }
   // consumers: start the scale / zero-point loads of every k-block now (up
-  // to 8 in flight per thread); they land in shared memory below
-  float sv[8], zv[8];
-  if (KIND != EE_W_DENSE && warp < 8) {
+  // to 4 in flight per thread); they land in shared memory below
+  float sv[4], zv[4];
+  if (KIND != EE_W_DENSE && warp < kStreamCWarps) {
     const int ng = L.k / L.group;
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = threadIdx.x + 256 * u;
+    for (int u = 0; u < 4; ++u) {
+      const int i = threadIdx.x + kStreamCThreads * u;
       sv[u] = zv[u] = 0.f;
       if (i < a.kbc * 128) {
         const int kb = i >> 7, r = i & 127;
@@ -116,16 +131,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
   }
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < a.nst; ++s) {
-      mbar_init(bar_full + 8u * s, 1);
-      mbar_init(bar_empty + 8u * s, 4);
-    }
-    mbar_fence_init();
-  }
   __syncthreads();
 
-  if (warp == 8) {
+  if (warp == kStreamCWarps) {
     // ---------------- producer: TMA loads into the ring ----------------
     if (lane == 0) {
       int issued = 0;
@@ -137,7 +145,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           break;
         }
         const uint32_t st = sb + (uint32_t)s * a.stage_bytes, fb = bar_full + 8u * s;
-        mbar_arrive_expect_tx(fb, WB + XB);
+        mbar_arrive_expect_tx(fb, a.xres ? WB : WB + XB);
         const int kabs = kb_first + kb;
         if (KIND == EE_W_DENSE) {
           tma_load_2d(st, &tw, kabs * 256, n0, fb);
@@ -145,8 +153,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         } else {
           tma_load_2d(st, &tw, kabs * (KIND == EE_W_INT8 ? 128 : 64), n0, fb);
         }
-        tma_load_2d(st + WB, &tx, kabs * 128, 0, fb);
-        tma_load_2d(st + WB + XB / 2, &tx, kabs * 128 + 64, 0, fb);
+        if (!a.xres) {
+          tma_load_2d(st + WB, &tx, kabs * 128, 0, fb);
+          tma_load_2d(st + WB + XB / 2, &tx, kabs * 128 + 64, 0, fb);
+        }
         ++issued;
       }
       if (!ok) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
@@ -164,8 +174,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const int nbase = n0 + rank * RS;
     if (KIND != EE_W_DENSE) {
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = threadIdx.x + 256 * u;
+      for (int u = 0; u < 4; ++u) {
+        const int i = threadIdx.x + kStreamCThreads * u;
         if (i < a.kbc * 128) {
           scal[i] = sv[u];
           if (KIND == EE_W_UINT4Z) zero[i] = zv[u];
@@ -176,10 +186,23 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       const int n = nbase + threadIdx.x;
       sbias[threadIdx.x] = (a.has_bias && n < L.n) ? ld_param(reinterpret_cast<const T*>(L.bias) + n) : 0.f;
     }
+    if (a.xres) {
+      // the CTA's activation slice, in the layout TMA would have produced
+      const char* xb = reinterpret_cast<const char*>(a.x);
+      const int per_kb = 2 * 8 * JT * 8;  // 16-byte chunks per k-block
+      for (int i = threadIdx.x; i < a.kbc * per_kb; i += kStreamCThreads) {
+        const int kb = i / per_kb, rem = i - kb * per_kb;
+        const int box = rem / (8 * JT * 8), rem2 = rem - box * (8 * JT * 8);
+        const int row = rem2 >> 3, cc = rem2 & 7;
+        const bool ok = row < a.M;
+        const char* src = xb + ((size_t)(ok ? row : 0) * a.ldx + (size_t)(kb_first + kb) * kKBlock + box * 64 + cc * 8) * 2;
+        cp_async16(sb + a.off_x + (uint32_t)(kb * 2 + box) * (XB / 2) + sw128(row, cc), src, ok);
+      }
+    }
     if (a.epi == EPI_RESID) {
       const int rcpr = RS / 8;
       const char* rb = reinterpret_cast<const char*>(a.resid);
-      for (int i = threadIdx.x; i < a.M * rcpr; i += 256) {
+      for (int i = threadIdx.x; i < a.M * rcpr; i += kStreamCThreads) {
         const int row = i / rcpr, c = i - row * rcpr;
         const bool ok = nbase + c * 8 + 8 <= L.n;
         const char* src = rb + ((size_t)row * a.ldr + (ok ? nbase + c * 8 : 0)) * 2;
@@ -188,17 +211,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
     cp_async_commit();
     cp_async_wait<0>();
-    named_sync(1, 256);
+    named_sync(1, kStreamCThreads);
 
-    const int rw = warp & 3, kg = warp >> 2;
+    const int rw = warp & 7, kg = warp >> 3;
     const int jt = min(JT, (a.M + 7) >> 3);  // active 8-token tiles
-    float acc[2][JT][4];
+    float acc[1][JT][4];
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
+    for (int j = 0; j < JT; ++j)
 #pragma unroll
-      for (int j = 0; j < JT; ++j)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[mi][j][c] = 0.f;
+      for (int c = 0; c < 4; ++c) acc[0][j][c] = 0.f;
 
     for (int kb = kg; kb < a.kbc; kb += 2) {
       const int s = kb % a.nst;
@@ -207,15 +228,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         break;
       }
       const uint32_t st = sb + (uint32_t)s * a.stage_bytes;
-      uint32_t A[2][8][4];
-      float sc[2][2];
+      uint32_t A[1][8][4];
+      float sc[1][2];
 #pragma unroll
-      for (int mi = 0; mi < 2; ++mi) {
+      for (int mi = 0; mi < 1; ++mi) {
         uint4 w[2][WPR];
         float z[2] = {0.f, 0.f};
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int r = 32 * rw + 16 * mi + g + 8 * h;
+          const int r = 16 * rw + g + 8 * h;
           if (KIND == EE_W_DENSE) {
 #pragma unroll
             for (int i = 0; i < 4; ++i)
@@ -233,7 +254,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         }
         Gemm<T, KIND>::dequant(w, z, A[mi]);
       }
-      const uint32_t xs = st + WB + (uint32_t)(t >> 1) * (XB / 2);
+      const uint32_t xs = (a.xres ? sb + a.off_x + (uint32_t)kb * XB : st + WB) + (uint32_t)(t >> 1) * (XB / 2);
 #pragma unroll
       for (int j = 0; j < JT; ++j) {
         if (j < jt) {
@@ -242,7 +263,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #pragma unroll
           for (int s2 = 0; s2 < 4; ++s2) xq[s2] = lds16(xs + sw128(row, (4 * t + s2) & 7));
 #pragma unroll
-          for (int mi = 0; mi < 2; ++mi) {
+          for (int mi = 0; mi < 1; ++mi) {
             if (KIND == EE_W_DENSE) {
 #pragma unroll
               for (int s = 0; s < 8; ++s)
@@ -274,13 +295,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const int qslot = rank * 2 + kg;
     const int rshift = 7 - a.lsplit;
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
+    for (int mi = 0; mi < 1; ++mi)
 #pragma unroll
       for (int j = 0; j < JT; ++j)
         if (j < jt) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int row = 32 * rw + 16 * mi + g + 8 * h;
+            const int row = 16 * rw + g + 8 * h;
             const int owner = row >> rshift, lrow = row & (RS - 1);
             const uint32_t off = (uint32_t)(((qslot * RS + lrow) * a.ps + 8 * j + 2 * t) * 4);
             st_dsmem_f2(mapa(recv + off, (uint32_t)owner), acc[mi][j][2 * h], acc[mi][j][2 * h + 1]);
@@ -289,13 +310,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   }
   cluster_sync();  // every partial of the unit has arrived; the ring is idle
 
-  if (warp < 8) {
+  if (warp < kStreamCWarps) {
     // sum the 2*S partials of this CTA's RS rows in slot order
     const int ntok = min(JT, (a.M + 7) >> 3) * 8;
     const float* R = reinterpret_cast<const float*>(smem + a.off_recv);
     float* E = reinterpret_cast<float*>(smem);  // [ntok][RS], reuses the ring
     const int nq = 2 * S;
-    for (int i = threadIdx.x; i < RS * (ntok >> 2); i += 256) {
+    for (int i = threadIdx.x; i < RS * (ntok >> 2); i += kStreamCThreads) {
       const int row = i % RS, c4 = i / RS;
       float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int q = 0; q < nq; ++q) {
@@ -310,7 +331,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       E[(4 * c4 + 2) * RS + row] = sum.z;
       E[(4 * c4 + 3) * RS + row] = sum.w;
     }
-    named_sync(1, 256);
+    named_sync(1, kStreamCThreads);
 
     // epilogue on 8-column chunks: bias, round, GELU / residual, 16-byte stores
     const ee_linear& Lw = a.w;
@@ -320,7 +341,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const int nbase = n0 + rank * RS;
     const int cpt = RS / 8;
     const bool vec = (a.ldo % 8) == 0;
-    for (int i = threadIdx.x; i < a.M * cpt; i += 256) {
+    for (int i = threadIdx.x; i < a.M * cpt; i += kStreamCThreads) {
       const int tok = i / cpt, ch = i - tok * cpt;
       const int nc = nbase + 8 * ch;
       if (nc >= Lw.n) continue;
@@ -370,13 +391,17 @@ int stream_launch_k(const GemmArgs& g, int* status, cudaStream_t st, bool* used)
   while (S > 1 && ((K % (kKBlock * S)) != 0 || U * S > dp->sms)) S >>= 1;
   const int lsplit = S == 8 ? 3 : (S == 4 ? 2 : (S == 2 ? 1 : 0));
   const int kbc = K / (kKBlock * S), RS = 128 / S;
-  if (kbc > 16) return EE_OK;  // scales are staged 8 per consumer thread
-  const uint32_t stage = align_up(stream_wbytes<KIND>() + 2048u * JT, 1024u);
+  if (kbc > 16) return EE_OK;  // scales are staged 4 per consumer thread
+  // few tokens: the activation slice stays resident (<= 64 KB)
+  const uint32_t xres_bytes = (uint32_t)kbc * 2048u * JT;
+  const int xres = (JT <= 4 && xres_bytes <= 65536u) ? 1 : 0;
+  const uint32_t stage = align_up(stream_wbytes<KIND>() + (xres ? 0u : 2048u * JT), 1024u);
   const int ps = 8 * JT + 4;
   const uint32_t scal = KIND == EE_W_DENSE ? 0u : (uint32_t)kbc * 128u * 4u * (KIND == EE_W_UINT4Z ? 2u : 1u);
   const uint32_t recv = 256u * ps * 4u;
   const uint32_t res = g.epi == EPI_RESID ? (uint32_t)(8 * JT * RS * 2) : 0u;
-  const uint32_t fixed = 16u * 8u + 16u + scal + 16u + recv + 16u + res + 16u + (uint32_t)RS * 4u + 1024u;
+  const uint32_t fixed = 16u * 8u + 16u + scal + 16u + recv + 16u + res + 16u + (uint32_t)RS * 4u + 1024u +
+                         (xres ? xres_bytes + 1024u : 0u);
   if ((uint32_t)dp->smem_optin <= fixed + stage) return EE_OK;
   int nst = (int)(((uint32_t)dp->smem_optin - fixed) / stage);
   nst = nst < 8 ? nst : 8;
@@ -405,7 +430,11 @@ int stream_launch_k(const GemmArgs& g, int* status, cudaStream_t st, bool* used)
   a.off_recv = align_up(a.off_scal + scal, 16u);
   a.off_res = align_up(a.off_recv + recv, 16u);
   a.off_bias = align_up(a.off_res + res, 16u);
-  const size_t smem = (size_t)a.off_bias + RS * 4 + 1024;
+  a.xres = xres;
+  a.x = g.x;
+  a.ldx = g.ldx;
+  a.off_x = align_up(a.off_bias + (uint32_t)RS * 4u, 1024u);
+  const size_t smem = (size_t)a.off_x + (xres ? xres_bytes : 0u) + 1024;
   if (smem > (size_t)dp->smem_optin) return EE_OK;
   a.status = status;
   a.timeout_ns = 1000000000ull;

@@ -90,6 +90,13 @@ def workload(cfg, seed: int = 0, batch: int = 1):
     return params, x0, prefix
 
 
+def fleet_request(cfg, r: int):
+    """Request r of the fleet: (prefix [1, P, d] bf16, x0 [1, H, A]) drawn from
+    ``torch.Generator().manual_seed(r)`` (noise first)."""
+    x0, pre = make_request(cfg, 1, torch.Generator().manual_seed(r))
+    return pre, x0
+
+
 def fleet_requests(cfg, n_requests: int, first: int = 0):
     """Fleet-mode inputs: request r draws its own x0 [1, H, A] and prefix [1, P, d]
     from ``torch.Generator().manual_seed(r)``."""
