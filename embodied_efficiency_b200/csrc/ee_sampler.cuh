@@ -2,8 +2,10 @@
 // sampler call (kernel/flow_expert.py:127-137 flow_sample over
 // ActionExpert.forward :117-124 and Block.forward :83-95).
 //
-// One CTA per SM in clusters of CL CTAs (cooperative launch). A call is a
-// fixed sequence of phases separated by a bounded grid barrier:
+// One CTA per SM in clusters of CL CTAs, the grid sized to the clusters
+// that can be resident at once (cudaOccupancyMaxActiveClusters), launched as a
+// plain cluster launch (the same launch eagerly and inside a CUDA graph). A
+// call is a fixed sequence of phases separated by a bounded grid barrier:
 //   EMB      time embedding of every step's t (t advanced in the act dtype)
 //   TPROJ    t_proj over all steps' embeddings at once (t does not depend on x)
 //   HEAD     step-0 in_proj + t_proj add (one CTA per token)
@@ -16,8 +18,9 @@
 //   TAIL     the last step's out_norm + out_proj + Euler update
 // GEMM phases are cluster split-K units (ee_gemm.cuh). The norms in front of
 // qkv / q_c / mlp0 are applied while those GEMMs stage their activation
-// slices, from per-token (sum, sum of squares) that the producing residual
-// phase accumulates atomically in its epilogue. Before each barrier a CTA
+// slices, from per-token (sum, sum of squares) partials that the producing
+// residual phase writes in its epilogue, one slot per 16 output columns,
+// summed by the consumer in a fixed order (deterministic). Before each barrier a CTA
 // starts copying the weights of its first unit of the next GEMM phase into
 // shared memory, so weight latency overlaps the barrier.
 #pragma once
@@ -692,20 +695,17 @@ int launch_sampler(Ctx c, cudaStream_t s) {
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = cl;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeCooperative;
-  attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  // Cooperative launch guarantees that every CTA is resident. Inside a stream
-  // capture the plain cluster launch is used: the grid is sized to what can be
-  // resident at once, and every barrier wait is bounded either way.
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(s, &cap) != cudaSuccess) return EE_ERR_LAUNCH;
-  cfg.numAttrs = cap == cudaStreamCaptureStatusNone ? 2 : 1;
+  // The grid never exceeds the clusters that fit on the device at once, so
+  // on a GPU not shared with concurrent kernels every CTA is resident; if one
+  // is not (another process holding SMs), the grid barrier's bounded wait
+  // ends the call with EE_ERR_TIMEOUT in the status word instead of hanging.
+  cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, fn_of<T, HD>(), c);
   return e == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
 }
