@@ -340,8 +340,10 @@ EE_DEV bool grid_barrier(unsigned* bar, int* abort_flag, int* status, unsigned l
   __syncthreads();
   if (threadIdx.x == 0) {
     int ok = 1;
-    __threadfence();
-    atomicAdd(bar, 1u);
+    // arrive with release semantics (orders this CTA's writes, made visible to
+    // thread 0 by the __syncthreads above, before the count); the polling
+    // loads below acquire, so no separate fences are needed
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(bar), "r"(1u) : "memory");
     const unsigned long long t0 = globaltimer();
     unsigned spins = 0;
     while (ld_acquire_gpu(bar) < target) {
@@ -358,7 +360,6 @@ EE_DEV bool grid_barrier(unsigned* bar, int* abort_flag, int* status, unsigned l
         }
       }
     }
-    __threadfence();
     s_ok = ok;
   }
   __syncthreads();
