@@ -65,7 +65,7 @@ struct GemmArgs {
 
 // Shared memory of a GEMM unit (byte offsets from the dynamic base).
 //   x    activation slice [64 tok][KS] (16-byte chunks swizzled, see
-//        x_chunk); after the MMAs it holds the reduced tile E[64][128/S]
+//        x_chunk); after the MMAs it holds the reduced tile E[64][128/S + 1]
 //   p    two receive buffers (alternating by round) for the partial tiles the
 //        sub-cluster's CTAs push here: [S][128/S rows][kPS] fp32 each
 //   aux  norm weight/bias slice, row statistics, bias, staged scales and the
@@ -437,26 +437,26 @@ struct Gemm {
             uint4 xq[4];
 #pragma unroll
             for (int s2 = 0; s2 < 4; ++s2) xq[s2] = lds16(rbase + x_chunk(row, 4 * t + s2) * 16);
-            if (KIND == EE_W_DENSE) {
+            // four independent accumulation chains of two MMAs each (chain c
+            // takes steps 2c and 2c+1, i.e. the k of xq[c]), so an MMA's
+            // latency is exposed twice per token tile, not eight times
+            float pc[4][4];
 #pragma unroll
-              for (int s = 0; s < 8; ++s)
-                mma16816<T>(acc[j], A[s][0], A[s][1], A[s][2], A[s][3], comp(xq[s >> 1], 2 * (s & 1)),
-                            comp(xq[s >> 1], 2 * (s & 1) + 1));
-            } else {
-              // two independent chains (steps 0-3, 4-7) halve the MMA dependency depth
-              float p[4] = {0.f, 0.f, 0.f, 0.f}, q[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
-              for (int s = 0; s < 4; ++s) {
-                mma16816<T>(p, A[s][0], A[s][1], A[s][2], A[s][3], comp(xq[s >> 1], 2 * (s & 1)),
-                            comp(xq[s >> 1], 2 * (s & 1) + 1));
-                mma16816<T>(q, A[s + 4][0], A[s + 4][1], A[s + 4][2], A[s + 4][3],
-                            comp(xq[(s + 4) >> 1], 2 * (s & 1)), comp(xq[(s + 4) >> 1], 2 * (s & 1) + 1));
+              for (int e = 0; e < 4; ++e) pc[cc][e] = 0.f;
+#pragma unroll
+            for (int hs = 0; hs < 2; ++hs)
+#pragma unroll
+              for (int cc = 0; cc < 4; ++cc) {
+                const int s = 2 * cc + hs;
+                mma16816<T>(pc[cc], A[s][0], A[s][1], A[s][2], A[s][3], comp(xq[cc], 2 * hs), comp(xq[cc], 2 * hs + 1));
               }
-              acc[j][0] += s0 * (p[0] + q[0]);
-              acc[j][1] += s0 * (p[1] + q[1]);
-              acc[j][2] += s1 * (p[2] + q[2]);
-              acc[j][3] += s1 * (p[3] + q[3]);
-            }
+            const float f0 = KIND == EE_W_DENSE ? 1.f : s0, f1 = KIND == EE_W_DENSE ? 1.f : s1;
+            acc[j][0] += f0 * ((pc[0][0] + pc[1][0]) + (pc[2][0] + pc[3][0]));
+            acc[j][1] += f0 * ((pc[0][1] + pc[1][1]) + (pc[2][1] + pc[3][1]));
+            acc[j][2] += f1 * ((pc[0][2] + pc[1][2]) + (pc[2][2] + pc[3][2]));
+            acc[j][3] += f1 * ((pc[0][3] + pc[1][3]) + (pc[2][3] + pc[3][3]));
           }
         }
       }
@@ -480,7 +480,8 @@ struct Gemm {
     cluster_sync();  // every partial of this round has arrived
 
     // 6. sum the S partials of this CTA's RPR rows (local, source order)
-    float* E = reinterpret_cast<float*>(smem + sm.x);  // [64][RPR], reuses the X slice
+    const int ES = RPR + 1;  // row stride of E (odd: the transposing writes below are conflict-free)
+    float* E = reinterpret_cast<float*>(smem + sm.x);  // [64][ES], reuses the X slice
     if (active) {
       const float* R = reinterpret_cast<const float*>(smem + sm.p + parity * kPBytes);
       for (int i = threadIdx.x; i < RPR * 16; i += kThreads) {
@@ -491,10 +492,10 @@ struct Gemm {
             const float4 v = *reinterpret_cast<const float4*>(R + (q * RPR + row) * kPS + 4 * c4);
             sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
           }
-          E[(4 * c4 + 0) * RPR + row] = sum.x;
-          E[(4 * c4 + 1) * RPR + row] = sum.y;
-          E[(4 * c4 + 2) * RPR + row] = sum.z;
-          E[(4 * c4 + 3) * RPR + row] = sum.w;
+          E[(4 * c4 + 0) * ES + row] = sum.x;
+          E[(4 * c4 + 1) * ES + row] = sum.y;
+          E[(4 * c4 + 2) * ES + row] = sum.z;
+          E[(4 * c4 + 3) * ES + row] = sum.w;
         }
       }
       __syncthreads();
@@ -512,7 +513,7 @@ struct Gemm {
         if (a.epi == EPI_RESID) rq = *reinterpret_cast<const uint4*>(sres + tok * RPR + 8 * ch);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          float y = Act<T>::round(E[tok * RPR + 8 * ch + e] + sbias[8 * ch + e]);
+          float y = Act<T>::round(E[tok * ES + 8 * ch + e] + sbias[8 * ch + e]);
           if (a.epi == EPI_GELU) {
             y = Act<T>::round(gelu_erf(y));
           } else if (a.epi == EPI_RESID) {
@@ -520,7 +521,7 @@ struct Gemm {
             y = Act<T>::round(((e & 1) ? rf.y : rf.x) + y);
           }
           v[e] = n0 + e < L.n ? y : 0.f;
-          E[tok * RPR + 8 * ch + e] = v[e];  // final values for the row statistics
+          E[tok * ES + 8 * ch + e] = v[e];  // final values for the row statistics
         }
         T* dst = out + (size_t)(m0 + tok) * a.ldo + n0;
         if (vec && n0 + 8 <= L.n) {
@@ -538,7 +539,7 @@ struct Gemm {
         if (threadIdx.x < mrows) {
           float sx = 0.f, sxx = 0.f;
           for (int col = 0; col < RPR; ++col) {
-            const float y = E[threadIdx.x * RPR + col];
+            const float y = E[threadIdx.x * ES + col];
             sx += y;
             sxx += y * y;
           }

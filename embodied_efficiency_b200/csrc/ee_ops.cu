@@ -60,7 +60,7 @@ static int launch_gemm_k(GemmArgs a, cudaStream_t s) {
   if (units > 0x7fffffffLL) return EE_ERR_SHAPE;
   const int rows8 = a.M >= kMTile ? kMTile : ((a.M + 7) / 8) * 8;
   size_t x = (size_t)rows8 * (a.w.k / cl) * 2;
-  const size_t e = (size_t)rows8 * (kRU / cl) * 4;
+  const size_t e = (size_t)rows8 * (kRU / cl + 1) * 4;
   if (e > x) x = e;
   x = (x + 127) & ~(size_t)127;
   GemmSmem sm;

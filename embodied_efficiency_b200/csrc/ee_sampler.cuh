@@ -533,7 +533,7 @@ struct SamplerSmem {
 
 inline SamplerSmem sampler_smem_map(const ee_expert& ex, int smem_optin) {
   size_t x = gemm_x_bytes(sampler_ks_cap(ex));
-  if (x < (size_t)kMTile * kRU * 4) x = (size_t)kMTile * kRU * 4;  // reduced tile E
+  if (x < (size_t)kMTile * (kRU + 1) * 4) x = (size_t)kMTile * (kRU + 1) * 4;  // reduced tile E
   const size_t rows = ((size_t)ex.d_model + 64) * 4;                // row phases
   if (rows > x) x = rows;
   x = (x + 127) & ~(size_t)127;

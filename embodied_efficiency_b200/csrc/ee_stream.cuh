@@ -264,25 +264,24 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           for (int s2 = 0; s2 < 4; ++s2) xq[s2] = lds16(xs + sw128(row, (4 * t + s2) & 7));
 #pragma unroll
           for (int mi = 0; mi < 1; ++mi) {
-            if (KIND == EE_W_DENSE) {
+            // four chains of two MMAs (chain c: steps 2c, 2c+1 = the k of xq[c])
+            float pc[4][4];
 #pragma unroll
-              for (int s = 0; s < 8; ++s)
-                mma16816<T>(acc[mi][j], A[mi][s][0], A[mi][s][1], A[mi][s][2], A[mi][s][3],
-                            comp(xq[s >> 1], 2 * (s & 1)), comp(xq[s >> 1], 2 * (s & 1) + 1));
-            } else {
-              float p[4] = {0.f, 0.f, 0.f, 0.f}, q[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
-              for (int s = 0; s < 4; ++s) {
-                mma16816<T>(p, A[mi][s][0], A[mi][s][1], A[mi][s][2], A[mi][s][3],
-                            comp(xq[s >> 1], 2 * (s & 1)), comp(xq[s >> 1], 2 * (s & 1) + 1));
-                mma16816<T>(q, A[mi][s + 4][0], A[mi][s + 4][1], A[mi][s + 4][2], A[mi][s + 4][3],
-                            comp(xq[(s + 4) >> 1], 2 * (s & 1)), comp(xq[(s + 4) >> 1], 2 * (s & 1) + 1));
+              for (int e = 0; e < 4; ++e) pc[cc][e] = 0.f;
+#pragma unroll
+            for (int hs = 0; hs < 2; ++hs)
+#pragma unroll
+              for (int cc = 0; cc < 4; ++cc) {
+                const int s = 2 * cc + hs;
+                mma16816<T>(pc[cc], A[mi][s][0], A[mi][s][1], A[mi][s][2], A[mi][s][3], comp(xq[cc], 2 * hs),
+                            comp(xq[cc], 2 * hs + 1));
               }
-              acc[mi][j][0] += sc[mi][0] * (p[0] + q[0]);
-              acc[mi][j][1] += sc[mi][0] * (p[1] + q[1]);
-              acc[mi][j][2] += sc[mi][1] * (p[2] + q[2]);
-              acc[mi][j][3] += sc[mi][1] * (p[3] + q[3]);
-            }
+            acc[mi][j][0] += sc[mi][0] * ((pc[0][0] + pc[1][0]) + (pc[2][0] + pc[3][0]));
+            acc[mi][j][1] += sc[mi][0] * ((pc[0][1] + pc[1][1]) + (pc[2][1] + pc[3][1]));
+            acc[mi][j][2] += sc[mi][1] * ((pc[0][2] + pc[1][2]) + (pc[2][2] + pc[3][2]));
+            acc[mi][j][3] += sc[mi][1] * ((pc[0][3] + pc[1][3]) + (pc[2][3] + pc[3][3]));
           }
         }
       }
