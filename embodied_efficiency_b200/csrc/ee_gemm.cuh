@@ -273,11 +273,23 @@ struct Gemm {
       // 1. activation slice, norm weight / bias slice, residual tile -> smem
       const int cpr = KS / 8;  // 16-byte chunks per token row
       const char* xb = reinterpret_cast<const char*>(a.x);
-      for (int i = threadIdx.x; i < JT * 8 * cpr; i += kThreads) {
-        const int row = i / cpr, c = i - row * cpr;
-        const bool ok = row < mrows;
-        const char* src = xb + ((size_t)(m0 + (ok ? row : 0)) * a.ldx + (size_t)kb0 * kKBlock + c * 8) * 2;
-        cp_async16(sx + (uint32_t)(row * KS * 2 + ((c >> 4) * 16 + x_chunk(row, c & 15)) * 16), src, ok);
+      if (kThreads % cpr == 0) {
+        // each thread keeps one chunk column and steps over rows: no per-chunk division
+        const int c = threadIdx.x % cpr, rstep = kThreads / cpr;
+        const char* src = xb + ((size_t)m0 * a.ldx + (size_t)kb0 * kKBlock + c * 8) * 2;
+        const size_t sstep = (size_t)a.ldx * 2;
+        for (int row = threadIdx.x / cpr; row < JT * 8; row += rstep) {
+          const bool ok = row < mrows;
+          cp_async16(sx + (uint32_t)(row * KS * 2 + ((c >> 4) * 16 + x_chunk(row, c & 15)) * 16),
+                     ok ? src + (size_t)row * sstep : src, ok);
+        }
+      } else {
+        for (int i = threadIdx.x; i < JT * 8 * cpr; i += kThreads) {
+          const int row = i / cpr, c = i - row * cpr;
+          const bool ok = row < mrows;
+          const char* src = xb + ((size_t)(m0 + (ok ? row : 0)) * a.ldx + (size_t)kb0 * kKBlock + c * 8) * 2;
+          cp_async16(sx + (uint32_t)(row * KS * 2 + ((c >> 4) * 16 + x_chunk(row, c & 15)) * 16), src, ok);
+        }
       }
       if (a.in_stats) {
         const uint32_t sg = sbase + sm.aux + kAuxGB;
@@ -379,8 +391,14 @@ struct Gemm {
         const int cpr = KS / 8;
         const T* sgw = reinterpret_cast<const T*>(aux + kAuxGB);
         const T* sgb = sgw + kMaxNormSlice;
-        for (int i = threadIdx.x; i < mrows * cpr; i += kThreads) {
-          const int row = i / cpr, pc = i - row * cpr;
+        const bool fixed_col = (kThreads % cpr) == 0;  // thread keeps one chunk column
+        const int rstep = fixed_col ? kThreads / cpr : 0;
+        for (int i = threadIdx.x, row = fixed_col ? threadIdx.x / cpr : 0, pc = fixed_col ? threadIdx.x % cpr : 0;
+             fixed_col ? row < mrows : i < mrows * cpr; i += kThreads, row += rstep) {
+          if (!fixed_col) {
+            row = i / cpr;
+            pc = i - row * cpr;
+          }
           const int c = (pc & ~15) + x_chunk(row, pc & 15);  // logical chunk of physical pc
           uint4* q = reinterpret_cast<uint4*>(smem + sm.x + row * KS * 2 + pc * 16);
           const uint4 v = *q;
