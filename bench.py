@@ -193,7 +193,7 @@ def gemm_sweep(device, flush):
     return out
 
 
-def fleet_run(expert, rank, world, dev, n_requests=256, chunk=32, steps=5, warmup=3):
+def fleet_run(expert, rank, world, dev, n_requests=256, chunk=256, steps=5, warmup=3):
     """Fleet mode: n_requests independent int4 sampler requests (request r
     seeded with r) sharded in contiguous blocks over the ranks, no collective;
     device time of one fleet step (every chunk of this rank), max over ranks."""
@@ -336,7 +336,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-fleet", action="store_true")
-    ap.add_argument("--fleet-chunk", type=int, default=32)
+    ap.add_argument("--fleet-chunk", type=int, default=256)
     ap.add_argument("--profile", default=None,
                     help="gemm:M:K:BITS or sampler:BITS -- a few launches for a profiler")
     args = ap.parse_args()

@@ -76,13 +76,20 @@ def _norm(cfg):
         else nn.LayerNorm(cfg.d_model)
 
 
-def _apply_linear(mod, x):
-    """A linear of the eager path on the sm_100a GEMM (cuBLAS only for K % 128 != 0)."""
-    if isinstance(mod, nn.Linear):
-        if mod.in_features % 128 == 0 and x.dtype in (torch.bfloat16, torch.float16):
-            return wq_linear(x, mod.weight, None, mod.bias, 0, 16)
-        return F.linear(x, mod.weight, mod.bias)
-    return mod(x)
+def _apply_linear(mod, x, gelu: bool = False, residual=None):
+    """A linear of the eager path on the sm_100a GEMM (cuBLAS only for K % 128 != 0),
+    with GELU or ``residual +`` fused into the GEMM epilogue (the same roundings
+    as the separate torch ops: bias add, round, then GELU or residual add, round)."""
+    fast = x.dtype in (torch.bfloat16, torch.float16)
+    if isinstance(mod, nn.Linear) and mod.in_features % 128 == 0 and fast:
+        return wq_linear(x, mod.weight, None, mod.bias, 0, 16, gelu=gelu, residual=residual)
+    if type(mod).__name__ == "TritonQuantLinear" and fast:
+        return wq_linear(x, mod.weight, mod.scales, mod.bias, mod.group_size, mod.bits, gelu=gelu,
+                         residual=residual)
+    y = F.linear(x, mod.weight, mod.bias) if isinstance(mod, nn.Linear) else mod(x)
+    if gelu:
+        y = F.gelu(y)
+    return y if residual is None else residual + y
 
 
 class Block(nn.Module):
@@ -129,12 +136,11 @@ class Block(nn.Module):
         if self.qkv is not None:
             q, k, v = _apply_linear(self.qkv, self.n1(x)).chunk(3, dim=-1)
             a = F.scaled_dot_product_attention(self._split(q), self._split(k), self._split(v))
-            x = x + _apply_linear(self.proj, self._merge(a))
+            x = _apply_linear(self.proj, self._merge(a), residual=x)
         q = self._split(_apply_linear(self.q_c, self.nx(x)))
         a = F.scaled_dot_product_attention(q, kv_c[0], kv_c[1])
-        x = x + _apply_linear(self.out_c, self._merge(a))
-        x = x + _apply_linear(self.mlp[2], F.gelu(_apply_linear(self.mlp[0], self.n2(x))))
-        return x
+        x = _apply_linear(self.out_c, self._merge(a), residual=x)
+        return _apply_linear(self.mlp[2], _apply_linear(self.mlp[0], self.n2(x), gelu=True), residual=x)
 
 
 class ActionExpert(nn.Module):
@@ -173,6 +179,11 @@ class ActionExpert(nn.Module):
         if _fused.supports(self, b):
             v = self.plan(b, prefix_kv).run(x_act, 1, t0=t, mode=_lib.EE_MODE_VELOCITY)
             return v.to(x_act.dtype)
+        return self.forward_layers(x_act, t, prefix_kv)
+
+    def forward_layers(self, x_act: torch.Tensor, t: torch.Tensor, prefix_kv):
+        """The same velocity computed layer by layer (sm_100a GEMMs with fused
+        GELU / residual epilogues, torch norms and attention between them)."""
         x = _apply_linear(self.in_proj, x_act)
         temb = _apply_linear(self.t_proj, timestep_embedding(t, self.cfg.d_model).to(x.dtype))
         x = x + temb[:, None, :]
@@ -208,21 +219,33 @@ def get_plan(expert, batch: int, prefix_kv):
     return pl
 
 
+# Token count (batch x horizon) up to which a sampler call runs as the single
+# fused launch; larger batches are GEMM-throughput work and run layer by layer
+# with the tcgen05 dequant-GEMM (GELU / residual in its epilogues).
+FUSED_MAX_TOKENS = 600
+
+
 @torch.no_grad()
-def flow_sample(expert, x_init: torch.Tensor, n_steps: int, prefix_kv) -> torch.Tensor:
+def flow_sample(expert, x_init: torch.Tensor, n_steps: int, prefix_kv, path: str = "auto") -> torch.Tensor:
     """kernel/flow_expert.py:127-137: Euler integration over n_steps, t in x.dtype.
 
-    On the fused path all n_steps run in one ``ee_flow_sample`` launch.
+    On the fused path all n_steps run in one ``ee_flow_sample`` launch. ``path``:
+    "auto" (fused up to FUSED_MAX_TOKENS tokens, else layer by layer), "fused"
+    or "layers".
     """
     _lib.require_cuda(x_init)
     b = x_init.shape[0]
-    if _fused.supports(expert, b):
+    fused_ok = _fused.supports(expert, b)
+    if path == "fused" and not fused_ok:
+        raise ValueError("the fused launch does not cover this expert / batch")
+    use_fused = fused_ok and (path == "fused" or (path == "auto" and b * expert.cfg.horizon <= FUSED_MAX_TOKENS))
+    if use_fused:
         return get_plan(expert, b, prefix_kv).run(x_init, n_steps).to(x_init.dtype)
     x = x_init
     dt = 1.0 / n_steps
     t = torch.zeros(x.shape[0], device=x.device, dtype=x.dtype)
     for _ in range(n_steps):
-        v = expert(x, t, prefix_kv)
+        v = expert.forward_layers(x, t, prefix_kv) if hasattr(expert, "forward_layers") else expert(x, t, prefix_kv)
         x = x + v * dt
         t = t + dt
     return x

@@ -4,8 +4,9 @@ Each request is one batch-1 sampler call with its own prefix and noise
 (``ActionExpert.sample(prefix, steps, x0)``); requests never exchange data, so
 the fleet is split into contiguous blocks of requests, one block per rank (one
 process per GPU), with no collective on the data path. Inside a rank the block
-runs as fused sampler launches over chunks of ``chunk`` requests (the batch of
-one ``ee_flow_sample`` call, so every GEMM of the call sees 50 * chunk tokens).
+runs as sampler calls over chunks of ``chunk`` requests (every GEMM of a call
+sees 50 * chunk tokens): small chunks as the single fused launch, large ones
+layer by layer on the tcgen05 dequant-GEMM (``flow_sample`` picks).
 Results come back through host memory; ``gather_results`` assembles the whole
 fleet on one rank over any process group (gloo included) when a caller wants
 it, and is not part of the timed path.
@@ -53,7 +54,7 @@ class FleetSampler:
     it (the host logic is then testable without a GPU).
     """
 
-    def __init__(self, n_requests: int, rank: int, world: int, chunk: int = 32, n_steps: int = 10,
+    def __init__(self, n_requests: int, rank: int, world: int, chunk: int = 256, n_steps: int = 10,
                  expert=None, sample_fn: Optional[Callable] = None, device=None):
         if (expert is None) == (sample_fn is None):
             raise ValueError("give exactly one of expert / sample_fn")

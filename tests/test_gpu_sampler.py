@@ -156,3 +156,29 @@ def test_plan_rejects_bad_inputs(cuda):
         flow_sample(m, torch.zeros(2, 50, 32, device=cuda, dtype=torch.bfloat16), 10, kv)
     with pytest.raises(RuntimeError):
         flow_sample(m, x0.bfloat16(), 10, kv)  # CPU input
+
+
+def test_layer_path_matches_fused_and_oracle(cuda):
+    """The layer-by-layer path (tcgen05 GEMMs, fused GELU / residual epilogues)
+    that large batches take agrees with the single fused launch and with the
+    oracle on the same requests."""
+    from embodied_efficiency_b200 import ActionExpert, ActionExpertConfig, flow_sample, quantize_model_triton, synth
+    from oracle import sampler as OS
+    cfg = ActionExpertConfig(d_model=256, n_layers=2, n_heads=4, prefix_len=32)
+    params, _, _ = synth.workload(cfg, seed=5)
+    m = ActionExpert(cfg)
+    m.load_state_dict(params)
+    m = m.to(cuda).bfloat16().eval()
+    quantize_model_triton(m, bits=4)
+    x0, pre = synth.fleet_requests(cfg, 16)
+    kv = m.encode(pre.to(cuda))
+    xb = x0.to(cuda).bfloat16()
+    lay = flow_sample(m, xb, 10, kv, path="layers").float().cpu()
+    fus = flow_sample(m, xb, 10, kv, path="fused").float().cpu()
+    assert float((lay - fus).abs().max() / fus.abs().max()) < 3e-2
+    ocfg = OS.Cfg(d_model=256, n_layers=2, n_heads=4, prefix_len=32)
+    p = {k: v.bfloat16() for k, v in params.items()}
+    qp = OS.quantize_params(p, ocfg, 4)
+    okv = OS.encode_prefix(p, ocfg, pre.bfloat16(), qp)
+    ref = OS.flow_sample(p, ocfg, x0.bfloat16(), 10, okv, qp).float()
+    assert OS.action_error(lay, ref) < 0.05
