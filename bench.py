@@ -133,7 +133,8 @@ def dist_setup(backend):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         import datetime
-        torch.distributed.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+        kw = {"device_id": torch.device("cuda", local)} if backend == "nccl" else {}
+        torch.distributed.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
     return rank, world, local
 
 

@@ -40,6 +40,10 @@ def supports(expert, batch: int) -> bool:
             return False
         if hid % 128:
             return False
+        # one CTA stages at most a 512-wide K slice (K split over a cluster of 8):
+        # the MLP down-projection's K (the hidden width) bounds the fused launch
+        if max(hid, d) > 8 * 512:
+            return False
         for blk in expert.blocks:
             mods = [blk.q_c, blk.out_c, blk.mlp[0], blk.mlp[2]]
             if getattr(blk, "qkv", None) is not None:

@@ -182,3 +182,23 @@ def test_layer_path_matches_fused_and_oracle(cuda):
     okv = OS.encode_prefix(p, ocfg, pre.bfloat16(), qp)
     ref = OS.flow_sample(p, ocfg, x0.bfloat16(), 10, okv, qp).float()
     assert OS.action_error(lay, ref) < 0.05
+
+
+def test_config5_scale_against_oracle(cuda):
+    """Pi0-scale expert (d 2048, 18 blocks, 16 x 128 heads, MLP 8192, prefix 816),
+    int4 group-128, batch 1, two Euler steps: action error against the oracle."""
+    from embodied_efficiency_b200 import ActionExpert, ActionExpertConfig, flow_sample, quantize_model_triton, synth
+    from oracle import sampler as OS
+    c5 = dict(d_model=2048, n_layers=18, n_heads=16, horizon=50, action_dim=32, prefix_len=816, mlp_ratio=4.0)
+    cfg = ActionExpertConfig(**c5)
+    params, x0, prefix = synth.workload(cfg, seed=0, batch=1)
+    m = ActionExpert(cfg)
+    m.load_state_dict(params)
+    m = m.to(cuda).bfloat16().eval()
+    quantize_model_triton(m, bits=4)
+    y = flow_sample(m, x0.to(cuda).bfloat16(), 2, m.encode(prefix.to(cuda))).float().cpu()
+    ocfg = OS.Cfg(**c5)
+    p = {k: v.bfloat16() for k, v in params.items()}
+    qp = OS.quantize_params(p, ocfg, 4)
+    ref = OS.flow_sample(p, ocfg, x0.bfloat16(), 2, OS.encode_prefix(p, ocfg, prefix.bfloat16(), qp), qp).float()
+    assert OS.action_error(y, ref) < 0.05
