@@ -138,9 +138,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     if (lane == 0) {
       int issued = 0;
       bool ok = true;
+      int s = 0, sph = 0;
       for (int kb = 0; kb < a.kbc; ++kb) {
-        const int s = kb % a.nst;
-        if (kb >= a.nst && !mbar_wait(bar_empty + 8u * s, ((kb / a.nst) - 1) & 1, a.timeout_ns)) {
+        if (kb >= a.nst && !mbar_wait(bar_empty + 8u * s, (uint32_t)(sph ^ 1), a.timeout_ns)) {
           ok = false;
           break;
         }
@@ -158,6 +158,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           tma_load_2d(st + WB + XB / 2, &tx, kabs * 128 + 64, 0, fb);
         }
         ++issued;
+        if (++s == a.nst) {
+          s = 0;
+          sph ^= 1;
+        }
       }
       if (!ok) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
       // every issued copy has landed before this CTA can leave
@@ -221,9 +225,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc[0][j][c] = 0.f;
 
+    int s = kg % a.nst, sph = (kg / a.nst) & 1;  // ring position of k-block kb (advanced below)
     for (int kb = kg; kb < a.kbc; kb += 2) {
-      const int s = kb % a.nst;
-      if (!mbar_wait(bar_full + 8u * s, (kb / a.nst) & 1, a.timeout_ns)) {
+      if (!mbar_wait(bar_full + 8u * s, (uint32_t)sph, a.timeout_ns)) {
         if (lane == 0) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
         break;
       }
@@ -287,6 +291,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_empty + 8u * s);
+      s += 2;
+      while (s >= a.nst) {
+        s -= a.nst;
+        sph ^= 1;
+      }
     }
 
     // push this warp's partial tile: rows of rank o go to rank o's receive area

@@ -69,13 +69,28 @@ __host__ __device__ constexpr uint32_t tc_tmem_cols(int nt) { return nt < 32 ? 3
 
 template <typename T, int KIND>
 struct TcDequant {
-  // Asynchronously copy the 4-byte word holding the scale (and zero point)
-  // of weight row n, absolute k-block kb, to shared memory (dst, dst + zoff).
-  // 16-bit values are fetched as their aligned 4-byte word; `hi` says which
-  // half holds the value.
-  static EE_DEV void stage_sz(const ee_linear& L, int n, int kb, uint32_t dst, uint32_t zoff) {
-    n = n < L.n ? n : L.n - 1;
-    const size_t si = (size_t)n * (L.k / L.group) + ((size_t)kb * kKBlock) / L.group;
+  // Scale (and zero point) element index of weight row n for group g is
+  // n * ng + g. The dequantising threads keep their rows' n * ng and find g
+  // from the absolute k-block without a division in the common cases.
+  struct Groups {
+    int ng;      // groups per row
+    int kpg;     // k-blocks per group
+    int shift;   // log2(kpg) when kpg is a power of two, else -1
+  };
+  static EE_DEV Groups groups(const ee_linear& L) {
+    Groups gp;
+    gp.ng = L.k / L.group;
+    gp.kpg = L.group / kKBlock;
+    gp.shift = (gp.kpg & (gp.kpg - 1)) == 0 ? __ffs(gp.kpg) - 1 : -1;
+    return gp;
+  }
+  static EE_DEV int group_of(const Groups& gp, int kb) {
+    return gp.ng == 1 ? 0 : (gp.shift >= 0 ? kb >> gp.shift : kb / gp.kpg);
+  }
+  // Asynchronously copy the 4-byte word holding element `si` of the scales
+  // (and zero points) to shared memory (dst, dst + zoff). 16-bit values are
+  // fetched as their aligned 4-byte word.
+  static EE_DEV void stage_sz(const ee_linear& L, size_t si, uint32_t dst, uint32_t zoff) {
     if (L.scale_dtype == EE_F32)
       cp_async4(dst, reinterpret_cast<const float*>(L.scales) + si);
     else
@@ -85,9 +100,7 @@ struct TcDequant {
   static EE_DEV float read_half(uint32_t word, bool hi) {
     return __half2float(__ushort_as_half((unsigned short)(hi ? (word >> 16) : (word & 0xFFFFu))));
   }
-  static EE_DEV void read_sz(const ee_linear& L, int n, int kb, uint32_t src, uint32_t zoff, float& s, float& z) {
-    n = n < L.n ? n : L.n - 1;
-    const size_t si = (size_t)n * (L.k / L.group) + ((size_t)kb * kKBlock) / L.group;
+  static EE_DEV void read_sz(const ee_linear& L, size_t si, uint32_t src, uint32_t zoff, float& s, float& z) {
     uint32_t w;
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w) : "r"(src));
     s = L.scale_dtype == EE_F32 ? __uint_as_float(w) : read_half(w, (si & 1) != 0);
@@ -168,9 +181,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       int issued = 0;
       bool ok = true;
+      int s = 0, sph = 0;
       for (int kb = 0; kb < a.kbc; ++kb) {
-        const int s = kb % a.ns;
-        if (kb >= a.ns && !mbar_wait(bar_empty + 8u * s, ((kb / a.ns) - 1) & 1, a.timeout_ns)) {
+        if (kb >= a.ns && !mbar_wait(bar_empty + 8u * s, (uint32_t)(sph ^ 1), a.timeout_ns)) {
           ok = false;
           break;
         }
@@ -186,6 +199,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tma_load_2d(st + WB, &tx, kabs * 128, m0, fb);
         tma_load_2d(st + WB + XB / 2, &tx, kabs * 128 + 64, m0, fb);
         ++issued;
+        if (++s == a.ns) { s = 0; sph ^= 1; }
       }
       if (!ok) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
       for (int kb = issued > a.ns ? issued - a.ns : 0; kb < issued; ++kb)
@@ -198,13 +212,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc<T>(128, NT);
       bool ok = true;
+      int s = 0, sph = 0, as = 0, aph = 0;
       for (int kb = 0; kb < a.kbc; ++kb) {
-        const int s = kb % a.ns, as = kb % a.na;
-        if (!mbar_wait(bar_full + 8u * s, (kb / a.ns) & 1, a.timeout_ns)) {
+        if (!mbar_wait(bar_full + 8u * s, (uint32_t)sph, a.timeout_ns)) {
           ok = false;
           break;
         }
-        if (DQ && !mbar_wait(bar_afull + 8u * as, (kb / a.na) & 1, a.timeout_ns)) {
+        if (DQ && !mbar_wait(bar_afull + 8u * as, (uint32_t)aph, a.timeout_ns)) {
           ok = false;
           break;
         }
@@ -222,6 +236,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         umma_commit(bar_empty + 8u * s);
         if (DQ) umma_commit(bar_aempty + 8u * as);
+        if (++s == a.ns) { s = 0; sph ^= 1; }
+        if (++as == a.na) { as = 0; aph ^= 1; }
       }
       if (!ok) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
       umma_commit(bar_acc);  // fires once every MMA issued above has completed
@@ -247,27 +263,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // a 3-slot ring of this thread's own words: [slot][item][thread]
       const uint32_t scr = sb + a.off_sc + (uint32_t)tid * 4u;
       constexpr uint32_t kSlot = (uint32_t)ITEMS * 256u * 4u, kZoff = 3u * kSlot;
+      const typename TcDequant<T, KIND>::Groups gp = TcDequant<T, KIND>::groups(L);
+      size_t rowsi[ITEMS];  // n * groups-per-row of each item's row
+#pragma unroll
+      for (int i = 0; i < ITEMS; ++i) rowsi[i] = (size_t)min(n0 + rows[i], L.n - 1) * gp.ng;
 #pragma unroll
       for (int d = 0; d < 2; ++d) {
         if (d < a.kbc) {
+          const int g = TcDequant<T, KIND>::group_of(gp, kb_first + d);
 #pragma unroll
           for (int i = 0; i < ITEMS; ++i)
-            TcDequant<T, KIND>::stage_sz(L, n0 + rows[i], kb_first + d, scr + (uint32_t)d * kSlot + (uint32_t)i * 1024u,
-                                         kZoff);
+            TcDequant<T, KIND>::stage_sz(L, rowsi[i] + g, scr + (uint32_t)d * kSlot + (uint32_t)i * 1024u, kZoff);
         }
         cp_async_commit();
       }
+      // ring positions advance by counters (no divisions in the loop)
+      int s = 0, sph = 0, as = 0, aph = 0, r3 = 0, r3n = 2;
       for (int kb = 0; kb < a.kbc; ++kb) {
-        const int s = kb % a.ns, as = kb % a.na;
         if (kb + 2 < a.kbc) {
+          const int g = TcDequant<T, KIND>::group_of(gp, kb_first + kb + 2);
 #pragma unroll
           for (int i = 0; i < ITEMS; ++i)
-            TcDequant<T, KIND>::stage_sz(L, n0 + rows[i], kb_first + kb + 2,
-                                         scr + (uint32_t)((kb + 2) % 3) * kSlot + (uint32_t)i * 1024u, kZoff);
+            TcDequant<T, KIND>::stage_sz(L, rowsi[i] + g, scr + (uint32_t)r3n * kSlot + (uint32_t)i * 1024u, kZoff);
         }
         cp_async_commit();
-        bool ok = mbar_wait(bar_full + 8u * s, (kb / a.ns) & 1, a.timeout_ns);
-        if (ok && kb >= a.na) ok = mbar_wait(bar_aempty + 8u * as, ((kb / a.na) - 1) & 1, a.timeout_ns);
+        bool ok = mbar_wait(bar_full + 8u * s, (uint32_t)sph, a.timeout_ns);
+        if (ok && kb >= a.na) ok = mbar_wait(bar_aempty + 8u * as, (uint32_t)(aph ^ 1), a.timeout_ns);
         if (!ok) {
           if (lane == 0) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
           break;
@@ -275,12 +296,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t st = sb + (uint32_t)s * a.stage_bytes;
         const uint32_t ab = sb + a.off_a + (uint32_t)as * 32768u;
         cp_async_wait<2>();  // this k-block's scale words have landed
+        const int gcur = TcDequant<T, KIND>::group_of(gp, kb_first + kb);
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) {
           const int row = rows[i], ch = chs[i];
           float scv, zcv;
-          TcDequant<T, KIND>::read_sz(L, n0 + row, kb_first + kb, scr + (uint32_t)(kb % 3) * kSlot + (uint32_t)i * 1024u,
-                                      kZoff, scv, zcv);
+          TcDequant<T, KIND>::read_sz(L, rowsi[i] + gcur, scr + (uint32_t)r3 * kSlot + (uint32_t)i * 1024u, kZoff,
+                                      scv, zcv);
           const uint32_t s2 = Act<T>::pack2(scv, scv);
           if (KIND == EE_W_INT8) {
             const uint4 raw = lds16(st + sw128(row, ch));
@@ -314,6 +336,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           mbar_arrive(bar_afull + 8u * as);
           mbar_arrive(bar_empty + 8u * s);
         }
+        if (++s == a.ns) { s = 0; sph ^= 1; }
+        if (++as == a.na) { as = 0; aph ^= 1; }
+        r3 = r3 == 2 ? 0 : r3 + 1;
+        r3n = r3n == 2 ? 0 : r3n + 1;
       }
       cp_async_wait<0>();
     }
