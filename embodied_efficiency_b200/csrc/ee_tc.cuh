@@ -3,23 +3,24 @@
 //
 // Tile: 128 weight rows (the MMA's M) x NT tokens (the MMA's N, 16..256)
 // over a K range, accumulated in fp32 in tensor memory. Roles inside a CTA
-// of 10 warps:
-//   warp 8      TMA producer: per k-block (128 k) one tile of raw weights in
+// of 18 warps:
+//   warp 16     TMA producer: per k-block (128 k) one tile of raw weights in
 //               the reference layout (int4 [128 rows x 64 B], 64-byte swizzle;
 //               int8 [128 x 128 B] and dense 16-bit [128 x 2 x 128 B],
 //               128-byte swizzle) and the activation tile [NT x 128 k]
 //               (two 64-k boxes, 128-byte swizzle) into a ring of `ns` stages;
-//   warps 0-7   dequantisers: raw weights -> q * scale in the activation
+//   warps 0-15  dequantisers (four per scheduler, so one warp's dependency
+//               stalls are covered by the others): raw weights -> q * scale in the activation
 //               dtype (the reference kernel's order: exact integer, times the
 //               scale rounded to the activation type, kernel/triton_gemm.py:
 //               91-94 and :127-134), written into a ring of `na` A tiles in
 //               the MMA's K-major 128-byte-swizzled layout; dense weights skip
 //               this step (TMA writes the A tile directly);
-//   warp 9      TMEM allocator and MMA issuer: one thread issues the eight
+//   warp 17     TMEM allocator and MMA issuer: one thread issues the eight
 //               M128 x N x K16 MMAs of each k-block and commits their
 //               completion to the barriers that free the stage and the A tile;
-//   warps 0-7   epilogue: TMEM -> registers (each warp its 32-lane quarter,
-//               half the columns), then either the final bias / GELU /
+//   warps 0-15  epilogue: TMEM -> registers (each warp its 32-lane quarter,
+//               a quarter of the columns), then either the final bias / GELU /
 //               residual and the store, or -- when K is split over the S CTAs
 //               of a cluster -- a push of the fp32 partial tile to the CTA
 //               owning those rows, a fixed-order sum there and the epilogue.
@@ -37,7 +38,10 @@
 
 namespace ee {
 
-constexpr int kTcWarps = 10;
+constexpr int kTcDqWarps = 16;  // dequantising / epilogue warps
+constexpr int kTcDqThreads = kTcDqWarps * 32;
+constexpr int kTcProdWarp = kTcDqWarps, kTcMmaWarp = kTcDqWarps + 1;
+constexpr int kTcWarps = kTcDqWarps + 2;
 constexpr int kTcThreads = kTcWarps * 32;
 
 struct TcArgs {
@@ -127,7 +131,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   constexpr uint32_t WB = tc_wbytes<KIND>();
   constexpr uint32_t XB = (uint32_t)NT * 256u;  // two boxes [NT rows][64 k]
   constexpr uint32_t TMC = tc_tmem_cols(NT);
-  constexpr int ITEMS = KIND == EE_W_INT8 ? 4 : 2;  // dequant items per thread per k-block
+  constexpr int ITEMS = KIND == EE_W_INT8 ? 2 : 1;  // dequant items per thread per k-block
   extern __shared__ __align__(1024) char smem_raw[];
   const uint32_t base0 = smem_u32(smem_raw);
   const uint32_t sb = (base0 + 1023u) & ~1023u;
@@ -151,23 +155,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t bar_aempty = bar_afull + 8u * a.na;
   const uint32_t bar_acc = bar_aempty + 8u * a.na;
 
-  if (warp == 8 && lane == 0) {
+  if (warp == kTcProdWarp && lane == 0) {
     tma_prefetch_map(&tw);
     tma_prefetch_map(&tx);
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.ns; ++s) {
       mbar_init(bar_full + 8u * s, 1);
-      mbar_init(bar_empty + 8u * s, DQ ? 9 : 1);  // 8 dequant warps + the MMA commit
+      mbar_init(bar_empty + 8u * s, DQ ? kTcDqWarps + 1 : 1);  // dequant warps + the MMA commit
     }
     for (int s = 0; s < a.na; ++s) {
-      mbar_init(bar_afull + 8u * s, 8);
+      mbar_init(bar_afull + 8u * s, kTcDqWarps);
       mbar_init(bar_aempty + 8u * s, 1);
     }
     mbar_init(bar_acc, 1);
     mbar_fence_init();
   }
-  if (warp == 9) {
+  if (warp == kTcMmaWarp) {
     tmem_alloc(sb + a.off_tm, TMC);
     tmem_relinquish();
   }
@@ -176,7 +180,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + a.off_tm);
 
-  if (warp == 8) {
+  if (warp == kTcProdWarp) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       int issued = 0;
@@ -207,7 +211,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
     }
     __syncwarp();
-  } else if (warp == 9) {
+  } else if (warp == kTcMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc<T>(128, NT);
@@ -244,13 +248,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- dequantisers (warps 0-7) ----------------
+    // ---------------- dequantisers (warps 0-15) ----------------
     if (DQ) {
       const int tid = threadIdx.x;
       int rows[ITEMS], chs[ITEMS];
 #pragma unroll
       for (int i = 0; i < ITEMS; ++i) {
-        const int q = tid + 256 * i;
+        const int q = tid + kTcDqThreads * i;
         if (KIND == EE_W_INT8) {
           rows[i] = (q & 7) + 8 * (q >> 6);
           chs[i] = (q >> 3) & 7;
@@ -262,7 +266,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // scales (and zero points) staged two k-blocks ahead with cp.async into
       // a 3-slot ring of this thread's own words: [slot][item][thread]
       const uint32_t scr = sb + a.off_sc + (uint32_t)tid * 4u;
-      constexpr uint32_t kSlot = (uint32_t)ITEMS * 256u * 4u, kZoff = 3u * kSlot;
+      constexpr uint32_t kSlot = (uint32_t)ITEMS * kTcDqThreads * 4u, kZoff = 3u * kSlot;
       const typename TcDequant<T, KIND>::Groups gp = TcDequant<T, KIND>::groups(L);
       size_t rowsi[ITEMS];  // n * groups-per-row of each item's row
 #pragma unroll
@@ -273,7 +277,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int g = TcDequant<T, KIND>::group_of(gp, kb_first + d);
 #pragma unroll
           for (int i = 0; i < ITEMS; ++i)
-            TcDequant<T, KIND>::stage_sz(L, rowsi[i] + g, scr + (uint32_t)d * kSlot + (uint32_t)i * 1024u, kZoff);
+            TcDequant<T, KIND>::stage_sz(L, rowsi[i] + g, scr + (uint32_t)d * kSlot + (uint32_t)i * (kTcDqThreads * 4u), kZoff);
         }
         cp_async_commit();
       }
@@ -284,7 +288,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int g = TcDequant<T, KIND>::group_of(gp, kb_first + kb + 2);
 #pragma unroll
           for (int i = 0; i < ITEMS; ++i)
-            TcDequant<T, KIND>::stage_sz(L, rowsi[i] + g, scr + (uint32_t)r3n * kSlot + (uint32_t)i * 1024u, kZoff);
+            TcDequant<T, KIND>::stage_sz(L, rowsi[i] + g, scr + (uint32_t)r3n * kSlot + (uint32_t)i * (kTcDqThreads * 4u), kZoff);
         }
         cp_async_commit();
         bool ok = mbar_wait(bar_full + 8u * s, (uint32_t)sph, a.timeout_ns);
@@ -301,7 +305,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = 0; i < ITEMS; ++i) {
           const int row = rows[i], ch = chs[i];
           float scv, zcv;
-          TcDequant<T, KIND>::read_sz(L, rowsi[i] + gcur, scr + (uint32_t)r3 * kSlot + (uint32_t)i * 1024u, kZoff,
+          TcDequant<T, KIND>::read_sz(L, rowsi[i] + gcur, scr + (uint32_t)r3 * kSlot + (uint32_t)i * (kTcDqThreads * 4u), kZoff,
                                       scv, zcv);
           const uint32_t s2 = Act<T>::pack2(scv, scv);
           if (KIND == EE_W_INT8) {
@@ -347,11 +351,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---------------- epilogue part 1: TMEM -> registers ----------------
     if (!mbar_wait(bar_acc, 0, a.timeout_ns) && lane == 0) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
     tc_fence_after();
-    const int q4 = warp & 3, half = warp >> 2;
+    const int q4 = warp & 3, quarter = warp >> 2;
     const int r = 32 * q4 + lane;  // weight row of the tile
     const int n = n0 + r;
-    constexpr int CPH = NT >= 32 ? NT / 2 : NT;  // columns per warp half
-    const int c_beg = half * CPH, c_end = (NT >= 32 || half == 0) ? c_beg + CPH : c_beg;
+    // columns split over the four warps of each lane quarter, 16 at a time
+    constexpr int NCH = NT / 16;                       // 16-column chunks
+    constexpr int CPQ = NCH >= 4 ? NCH / 4 : 1;        // chunks per warp
+    const int c_beg = quarter * CPQ * 16;
+    const int c_end = quarter < NCH ? c_beg + CPQ * 16 : c_beg;
     const int RS = 128 >> a.lsplit;
     if (S == 1) {
       const float bias = (a.has_bias && n < L.n) ? ld_param(reinterpret_cast<const T*>(L.bias) + n) : 0.f;
@@ -394,18 +401,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   tc_fence_before();
   cluster_sync();  // partials delivered; MMAs, copies and TMEM reads finished
-  if (warp == 9) {
+  if (warp == kTcMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, TMC);
   }
-  if (S > 1 && warp < 8) {
+  if (S > 1 && warp < kTcDqWarps) {
     // ---------------- epilogue part 2: owner sums the S partials ----------------
     const int RS = 128 >> a.lsplit;
     const int ntok = min(NT, a.M - m0);
     const int ntok4 = (ntok + 3) & ~3;
     const float* R = reinterpret_cast<const float*>(smem + a.off_recv);
     float* E = reinterpret_cast<float*>(smem);  // [ntok4][RS], reuses the stage ring
-    for (int i = threadIdx.x; i < RS * (ntok4 >> 2); i += 256) {
+    for (int i = threadIdx.x; i < RS * (ntok4 >> 2); i += kTcDqThreads) {
       const int row = i % RS, c4 = i / RS;
       float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int q = 0; q < S; ++q) {
@@ -420,13 +427,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       E[(4 * c4 + 2) * RS + row] = sum.z;
       E[(4 * c4 + 3) * RS + row] = sum.w;
     }
-    named_sync(1, 256);
+    named_sync(1, kTcDqThreads);
     const int nbase = n0 + rank * RS;
     const int cpt = RS / 8;
     const bool vec = (a.ldo % 8) == 0;
     T* out = reinterpret_cast<T*>(a.out);
     const T* res = reinterpret_cast<const T*>(a.resid);
-    for (int i = threadIdx.x; i < ntok * cpt; i += 256) {
+    for (int i = threadIdx.x; i < ntok * cpt; i += kTcDqThreads) {
       const int tok = i / cpt, ch = i - tok * cpt;
       const int nc = nbase + 8 * ch;
       if (nc >= L.n) continue;
@@ -514,7 +521,7 @@ int tc_launch_k(const GemmArgs& g, const TcShape& sh, int* status, cudaStream_t 
   const int ps = NT + 4;
   const uint32_t recv = S > 1 ? (uint32_t)(S * RS * ps * 4) : 0u;
   const int na = dq ? 2 : 0;
-  const uint32_t fixed = (uint32_t)na * 32768u + 8u * 40u + 16u + recv + 16u + 1024u + 3u * 4u * 256u * 4u * 2u + 16u;
+  const uint32_t fixed = (uint32_t)na * 32768u + 8u * 40u + 16u + recv + 16u + 1024u + 3u * 2u * kTcDqThreads * 4u * 2u + 16u;
   if ((uint32_t)dp->smem_optin <= fixed + stage) return EE_OK;
   int ns = (int)(((uint32_t)dp->smem_optin - fixed) / stage);
   ns = ns < 8 ? ns : 8;
@@ -545,8 +552,8 @@ int tc_launch_k(const GemmArgs& g, const TcShape& sh, int* status, cudaStream_t 
   a.off_bar = tc_align(ring_end, 16u);
   a.off_tm = a.off_bar + 8u * (2u * ns + 2u * (uint32_t)a.na + 1u);
   a.off_recv = tc_align(a.off_tm + 4u, 16u);
-  constexpr uint32_t items = KIND == EE_W_INT8 ? 4u : 2u;
-  const uint32_t scbytes = dq ? 3u * items * 256u * 4u * (KIND == EE_W_UINT4Z ? 2u : 1u) : 0u;
+  constexpr uint32_t items = KIND == EE_W_INT8 ? 2u : 1u;
+  const uint32_t scbytes = dq ? 3u * items * kTcDqThreads * 4u * (KIND == EE_W_UINT4Z ? 2u : 1u) : 0u;
   a.off_sc = tc_align(a.off_recv + recv, 16u);
   const size_t smem = (size_t)a.off_sc + scbytes + 1024;
   if (smem > (size_t)dp->smem_optin) return EE_OK;
