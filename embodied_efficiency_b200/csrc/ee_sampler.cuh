@@ -191,51 +191,97 @@ EE_DEV float block_sum(float v, float* scratch /* [kWarps] */) {
   return r;
 }
 
+// Two sums over the CTA at once (one pair of __syncthreads).
+EE_DEV float2 block_sum2(float a, float b, float* scratch /* [2 * kWarps] */) {
+  a = warp_sum(a);
+  b = warp_sum(b);
+  if ((threadIdx.x & 31) == 0) {
+    scratch[threadIdx.x >> 5] = a;
+    scratch[kWarps + (threadIdx.x >> 5)] = b;
+  }
+  __syncthreads();
+  float ra = 0.f, rb = 0.f;
+#pragma unroll
+  for (int i = 0; i < kWarps; ++i) {
+    ra += scratch[i];
+    rb += scratch[kWarps + i];
+  }
+  __syncthreads();
+  return make_float2(ra, rb);
+}
+
 // Token row m at `step`: (tail) out_norm + out_proj + Euler update or
 // velocity store, then (head) x = in_proj(x_act) + b + temb(next step) with
-// its row statistics for the next first norm. Shared memory: d + 48 floats.
+// its row statistics for the next first norm. Every load that does not
+// depend on this phase's arithmetic (the x row, the out_norm parameters, the
+// out_proj weights -- copied into the idle partial-tile buffers -- and the
+// Euler source values) is issued at entry.
+// Shared memory: d + 64 floats in the x region, out_proj in the p region.
 template <typename T>
 EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head, char* smem) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int d = c.ex.d_model, A = c.ex.action_dim, nch = d / 8;
   float* hrow = reinterpret_cast<float*>(smem + c.sm.x);  // [d]
-  float* xa = hrow + d;                                    // [32]
-  float* red = xa + 32;                                    // [kWarps]
+  float* xa = hrow + d;                                    // [32] action row after the update
+  float* xs = xa + 32;                                     // [32] Euler source values
+  float* red = xs + 32;                                    // [2 * kWarps]
   const int head_step = do_tail ? step + 1 : 0;
+
+  // ---- 1. loads that do not depend on this phase's arithmetic ----
+  uint4 xq = make_uint4(0, 0, 0, 0), wq = xq, bq = xq;
+  const T* Wo = reinterpret_cast<const T*>(c.ex.out_proj.weight);
+  const bool wo_smem = do_tail && (size_t)A * d * 2 <= 2 * kPBytes;
+  const uint32_t wo_s = smem_u32(smem) + c.sm.p;
   if (do_tail) {
-    // out_norm of x[m], rounded to the act dtype (the module output)
-    float v[8];
-    const T* xr = reinterpret_cast<const T*>(c.x) + (size_t)m * d;
-    float s = 0.f;
     if (tid < nch) {
-      const uint4 q = ld_act16(xr + tid * 8);
+      xq = ld_act16(reinterpret_cast<const T*>(c.x) + (size_t)m * d + tid * 8);
+      wq = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(c.ex.out_norm.weight) + tid * 8));
+      if (c.ex.out_norm.bias)
+        bq = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(c.ex.out_norm.bias) + tid * 8));
+    }
+    if (wo_smem) {
+      for (int i = tid; i < A * nch; i += kThreads) cp_async16(wo_s + (uint32_t)i * 16u, Wo + (size_t)i * 8, true);
+      cp_async_commit();
+    }
+    if (tid < A && c.mode != EE_MODE_VELOCITY) {
+      const T* src = step == 0 ? reinterpret_cast<const T*>(c.x_in) : reinterpret_cast<const T*>(c.x_out);
+      xs[tid] = Act<T>::to_f(*reinterpret_cast<const T*>(reinterpret_cast<const char*>(src) +
+                                                           ((size_t)m * A + tid) * sizeof(T)));
+    }
+  }
+  const int bb = m / c.ex.horizon;
+  const int trow = head_step * c.nbt + (c.nbt > 1 ? bb : 0);
+  const T* Wi = reinterpret_cast<const T*>(c.ex.in_proj.weight);
+  const T* bi = reinterpret_cast<const T*>(c.ex.in_proj.bias);
+  const T* temb = reinterpret_cast<const T*>(c.temb) + (size_t)trow * d;
+
+  if (do_tail) {
+    // ---- 2. out_norm of x[m] (one fused sum / sum-of-squares reduction) ----
+    float v[8];
+    float s1 = 0.f, s2 = 0.f;
+    if (tid < nch) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float2 f = Act<T>::unpack2(comp(q, e));
+        const float2 f = Act<T>::unpack2(comp(xq, e));
         v[2 * e] = f.x;
         v[2 * e + 1] = f.y;
       }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) s += c.ex.norm_kind == EE_NORM_RMS ? v[e] * v[e] : v[e];
+      for (int e = 0; e < 8; ++e) {
+        s1 += v[e];
+        s2 += v[e] * v[e];
+      }
     }
-    s = block_sum(s, red);
+    const float2 tot = block_sum2(s1, s2, red);
     const float inv_d = 1.0f / (float)d;
     float mean = 0.f, rstd;
     if (c.ex.norm_kind == EE_NORM_RMS) {
-      rstd = 1.0f / sqrtf(s * inv_d + c.ex.eps);
+      rstd = 1.0f / sqrtf(tot.y * inv_d + c.ex.eps);
     } else {
-      mean = s * inv_d;
-      float q2 = 0.f;
-      if (tid < nch)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) q2 += (v[e] - mean) * (v[e] - mean);
-      rstd = 1.0f / sqrtf(block_sum(q2, red) * inv_d + c.ex.eps);
+      mean = tot.x * inv_d;
+      rstd = 1.0f / sqrtf(fmaxf(tot.y * inv_d - mean * mean, 0.f) + c.ex.eps);
     }
     if (tid < nch) {
-      const T* w = reinterpret_cast<const T*>(c.ex.out_norm.weight);
-      const T* b = reinterpret_cast<const T*>(c.ex.out_norm.bias);
-      const uint4 wq = __ldg(reinterpret_cast<const uint4*>(w + tid * 8));
-      const uint4 bq = b ? __ldg(reinterpret_cast<const uint4*>(b + tid * 8)) : make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 wf = Act<T>::unpack2(comp(wq, e));
@@ -252,9 +298,9 @@ EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head,
         hrow[tid * 8 + 2 * e + 1] = Act<T>::round(y1);
       }
     }
+    if (wo_smem) cp_async_wait<0>();
     __syncthreads();
-    // out_proj: warp w computes outputs a = w, w+8, w+16, w+24
-    const T* W = reinterpret_cast<const T*>(c.ex.out_proj.weight);
+    // ---- 3. out_proj: warp w computes outputs a = w, w+8, w+16, w+24 ----
     const T* ob = reinterpret_cast<const T*>(c.ex.out_proj.bias);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -262,7 +308,7 @@ EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head,
       if (a < A) {
         float acc = 0.f;
         for (int ch = lane; ch < nch; ch += 32) {
-          const uint4 wv = ld_weight16(W + (size_t)a * d + ch * 8);
+          const uint4 wv = wo_smem ? lds16(wo_s + (uint32_t)(a * nch + ch) * 16u) : ld_weight16(Wo + (size_t)a * d + ch * 8);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f = Act<T>::unpack2(comp(wv, e));
@@ -277,8 +323,7 @@ EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head,
           if (c.mode == EE_MODE_VELOCITY) {
             *xo = Act<T>::from_f(vel);
           } else {
-            const T* src = step == 0 ? reinterpret_cast<const T*>(c.x_in) + (size_t)m * A + a : xo;
-            const float xnew = Act<T>::round(Act<T>::to_f(*src) + Act<T>::round(vel * c.dtf));
+            const float xnew = Act<T>::round(xs[a] + Act<T>::round(vel * c.dtf));
             *xo = Act<T>::from_f(xnew);
             xa[a] = xnew;
           }
@@ -290,42 +335,40 @@ EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head,
   }
   if (!do_head) return;
   __syncthreads();
-  // in_proj + bias + t_proj(temb) for the head step; row statistics
-  const int bb = m / c.ex.horizon;
-  const int trow = head_step * c.nbt + (c.nbt > 1 ? bb : 0);
-  const T* Wi = reinterpret_cast<const T*>(c.ex.in_proj.weight);
-  const T* bi = reinterpret_cast<const T*>(c.ex.in_proj.bias);
-  const T* temb = reinterpret_cast<const T*>(c.temb) + (size_t)trow * d;
+  // ---- 4. in_proj + bias + t_proj(temb) for the head step; row statistics ----
   T* xr = reinterpret_cast<T*>(c.x) + (size_t)m * d;
   float s = 0.f, ss = 0.f;
-  for (int n = tid; n < d; n += kThreads) {
-    const T* wr = Wi + (size_t)n * A;
+  auto one = [&](int n, const uint4 (&w4)[4], float bias, float tv) {
     float acc = 0.f;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       if (q * 8 < A) {
-        const uint4 wv = ld_weight16(wr + 8 * q);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float2 f = Act<T>::unpack2(comp(wv, e));
+          const float2 f = Act<T>::unpack2(comp(w4[q], e));
           acc = fmaf(xa[8 * q + 2 * e], f.x, acc);
           acc = fmaf(xa[8 * q + 2 * e + 1], f.y, acc);
         }
       }
     }
-    if (bi) acc += ld_param(bi + n);
-    const float y = Act<T>::round(Act<T>::round(acc) + ld_act_scalar(temb + n));
+    acc += bias;
+    const float y = Act<T>::round(Act<T>::round(acc) + tv);
     xr[n] = Act<T>::from_f(y);
     s += y;
     ss += y * y;
+  };
+  for (int n = tid; n < d; n += kThreads) {
+    uint4 w4[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) w4[q] = q * 8 < A ? ld_weight16(Wi + (size_t)n * A + 8 * q) : make_uint4(0, 0, 0, 0);
+    one(n, w4, bi ? ld_param(bi + n) : 0.f, ld_act_scalar(temb + n));
   }
-  s = block_sum(s, red);
-  ss = block_sum(ss, red);
+  const float2 tot = block_sum2(s, ss, red);
   // slot 0 holds the whole row, the other slots are zero
   float* st = stats_of(c, head_step, 0) + 2 * (size_t)m * c.n_slots;
   if (tid < c.n_slots) {
-    st[2 * tid] = tid == 0 ? s : 0.f;
-    st[2 * tid + 1] = tid == 0 ? ss : 0.f;
+    st[2 * tid] = tid == 0 ? tot.x : 0.f;
+    st[2 * tid + 1] = tid == 0 ? tot.y : 0.f;
   }
 }
 
@@ -534,7 +577,7 @@ struct SamplerSmem {
 inline SamplerSmem sampler_smem_map(const ee_expert& ex, int smem_optin) {
   size_t x = gemm_x_bytes(sampler_ks_cap(ex));
   if (x < (size_t)kMTile * (kRU + 1) * 4) x = (size_t)kMTile * (kRU + 1) * 4;  // reduced tile E
-  const size_t rows = ((size_t)ex.d_model + 64) * 4;                // row phases
+  const size_t rows = ((size_t)ex.d_model + 128) * 4;               // row phases
   if (rows > x) x = rows;
   x = (x + 127) & ~(size_t)127;
   SamplerSmem sm;
