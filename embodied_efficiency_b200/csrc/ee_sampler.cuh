@@ -412,6 +412,37 @@ EE_DEV bool grid_barrier(const Ctx& c, unsigned target) {
   return grid_barrier(c.bar, c.abort_flag, c.status, c.timeout_ns, target);
 }
 
+// Split form of the barrier: arrive (after a __syncthreads that ends the
+// phase), do work that needs no other CTA's results, then wait.
+EE_DEV void grid_arrive(const Ctx& c) {
+  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(c.bar), "r"(1u) : "memory");
+}
+EE_DEV bool grid_wait(const Ctx& c, unsigned target) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const unsigned long long t0 = globaltimer();
+    unsigned spins = 0;
+    while (ld_acquire_gpu(c.bar) < target) {
+      if ((++spins & 63u) == 0) {
+        if (ld_volatile_i32(c.abort_flag)) {
+          ok = 0;
+          break;
+        }
+        if (globaltimer() - t0 > c.timeout_ns) {
+          atomicCAS(c.status, 0, (int)EE_ERR_TIMEOUT);
+          atomicExch(c.abort_flag, 1);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
 template <typename T, int HD>
 __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_constant__ Ctx c) {
   extern __shared__ __align__(128) char smem[];
@@ -505,11 +536,14 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
     if (c.trace && threadIdx.x == 0)
       c.trace[((size_t)p * gridDim.x + blockIdx.x) * 2] = globaltimer();
     if (p + 1 < P) {
+      // arrive first, then start the next GEMM phase's weight copies while
+      // the other CTAs finish (the copies read only constant weights)
+      grid_arrive(c);
+      target += gridDim.x;
       const Phase nx = decode(c, p + 1);
       if (nx.type == PH_GEMM || nx.type == PH_TPROJ)
         have_pre = gemm_dispatch<T>(make_gemm(c, nx, smem), smem, c.sm, nullptr, true, &pre);
-      target += gridDim.x;
-      if (!grid_barrier(c, target)) {
+      if (!grid_wait(c, target)) {
         cp_async_wait<0>();
         return;
       }
