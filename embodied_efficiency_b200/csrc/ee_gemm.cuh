@@ -127,6 +127,7 @@ EE_DEV int x_chunk(int row, int c) { return c ^ (((c >> 3) & 1) << 1) ^ (row & 1
 struct PreRegs {
   float s[2];
   float z[2];
+  int aux;  // the unit's constant operands (norm slice, scales, bias) are staged too
 };
 
 template <typename T, int KIND>
@@ -209,8 +210,8 @@ struct Gemm {
 
   // Start copying this CTA's first k-blocks of n-tile `nt` into the pre area
   // (one cp.async group); scales of the first k-block go to pr.
-  static EE_DEV void prefetch(const GemmArgs& a, int nt, const GemmSmem& sm, uint32_t sbase,
-                              PreRegs& pr) {
+  static EE_DEV void prefetch(const GemmArgs& a, int nt, const GemmSmem& sm, char* smem, PreRegs& pr) {
+    const uint32_t sbase = smem_u32(smem);
     const int rank = (int)cl_rank();
     const int KB = (a.w.k >> a.lsplit) / kKBlock, kb0 = (rank & (a.split - 1)) * KB;
     const int fit = (int)(sm.pre_bytes / pre_kb_bytes(KIND));
@@ -225,7 +226,54 @@ struct Gemm {
       }
 #pragma unroll
     for (int h = 0; h < 2; ++h) load_scales(a.w, nw + g + 8 * h, kb0, pr.s[h], pr.z[h]);
+    stage_const(a, nt, sm, smem);
     cp_async_commit();
+    pr.aux = 1;
+  }
+
+  // The unit's operands that no other CTA produces -- the norm weight / bias
+  // slice, the fp32 scales of every k-block, the bias -- into the aux area
+  // (cp.async, committed by the caller; the bias with plain loads).
+  static EE_DEV void stage_const(const GemmArgs& a, int nt, const GemmSmem& sm, char* smem) {
+    const uint32_t sbase = smem_u32(smem);
+    const ee_linear& L = a.w;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int rank = (int)cl_rank(), r = rank & (a.split - 1);
+    const int KS = L.k >> a.lsplit, KB = KS / kKBlock, kb0 = r * KB;
+    const int RPR = kRU >> a.lsplit;
+    const int nw = nt * kRU + 16 * warp, nbase = nt * kRU + r * RPR;
+    if (a.in_stats) {
+      const int cpr = KS / 8;
+      const uint32_t sg = sbase + sm.aux + kAuxGB;
+      for (int i = threadIdx.x; i < 2 * cpr; i += kThreads) {
+        const int which = i / cpr, c = i - which * cpr;
+        const void* vec = which == 0 ? a.in_w : a.in_b;
+        const bool ok = vec != nullptr;
+        const char* src = reinterpret_cast<const char*>(ok ? vec : a.in_w) + ((size_t)kb0 * kKBlock + c * 8) * 2;
+        cp_async16(sg + (uint32_t)((which * kMaxNormSlice + c * 8) * 2), src, ok);
+      }
+    }
+    const bool smem_scales = KIND != EE_W_DENSE && L.scale_dtype == EE_F32 && KB <= kMaxKB;
+    if (smem_scales && t == 0) {
+      const int ng = L.k / L.group;
+      const float* sp = reinterpret_cast<const float*>(L.scales);
+      for (int kb = 0; kb < KB; ++kb)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          int n = nw + g + 8 * h;
+          n = n < L.n ? n : L.n - 1;
+          cp_async4(sbase + sm.aux + kAuxScale + (uint32_t)((((kb * 2 + h) * kWarps + warp) * 8 + g) * 4),
+                    sp + (size_t)n * ng + ((kb0 + kb) * kKBlock) / L.group);
+        }
+    }
+    // the last RPR threads load the bias (blocking loads): thread 0 stays free
+    // to poll the grid barrier when this runs between its arrive and wait
+    const int bt = threadIdx.x - (kThreads - RPR);
+    if (bt >= 0) {
+      float* sbias = reinterpret_cast<float*>(smem + sm.aux + kAuxBias);
+      const int n = nbase + bt;
+      sbias[bt] = (a.has_bias && n < L.n) ? ld_param(reinterpret_cast<const T*>(L.bias) + n) : 0.f;
+    }
   }
 
   // One unit: rows nt*128 .. +127 x tokens m0 .. m0+63 over all of K, by the S
@@ -260,7 +308,7 @@ struct Gemm {
     PreRegs pr_local;
     const PreRegs* prw = pre;
     if (active && !pre && sm.pre_bytes >= pre_kb_bytes(KIND)) {
-      prefetch(a, nt, sm, sbase, pr_local);
+      prefetch(a, nt, sm, smem, pr_local);
       prw = &pr_local;
     }
     const int fit = (int)(sm.pre_bytes / pre_kb_bytes(KIND));
@@ -291,16 +339,7 @@ struct Gemm {
           cp_async16(sx + (uint32_t)(row * KS * 2 + ((c >> 4) * 16 + x_chunk(row, c & 15)) * 16), src, ok);
         }
       }
-      if (a.in_stats) {
-        const uint32_t sg = sbase + sm.aux + kAuxGB;
-        for (int i = threadIdx.x; i < 2 * cpr; i += kThreads) {
-          const int which = i / cpr, c = i - which * cpr;
-          const void* vec = which == 0 ? a.in_w : a.in_b;
-          const bool ok = vec != nullptr;
-          const char* src = reinterpret_cast<const char*>(ok ? vec : a.in_w) + ((size_t)kb0 * kKBlock + c * 8) * 2;
-          cp_async16(sg + (uint32_t)((which * kMaxNormSlice + c * 8) * 2), src, ok);
-        }
-      }
+      if (!(prw && prw->aux)) stage_const(a, nt, sm, smem);  // else staged before the barrier
       if (a.epi == EPI_RESID) {
         const int rcpr = RPR / 8;  // 16-byte chunks of a residual row segment
         const char* rb = reinterpret_cast<const char*>(a.resid);
@@ -311,23 +350,7 @@ struct Gemm {
           cp_async16(sbase + sm.aux + kAuxRes + (uint32_t)((row * RPR + c * 8) * 2), src, ok);
         }
       }
-      if (smem_scales && t == 0) {
-        const int ng = L.k / L.group;
-        const float* sp = reinterpret_cast<const float*>(L.scales);
-        for (int kb = 0; kb < KB; ++kb)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            int n = nw + g + 8 * h;
-            n = n < L.n ? n : L.n - 1;
-            cp_async4(sbase + sm.aux + kAuxScale + (uint32_t)((((kb * 2 + h) * kWarps + warp) * 8 + g) * 4),
-                      sp + (size_t)n * ng + ((kb0 + kb) * kKBlock) / L.group);
-          }
-      }
       cp_async_commit();
-      if (threadIdx.x < RPR) {
-        const int n = nbase + threadIdx.x;
-        sbias[threadIdx.x] = (a.has_bias && n < L.n) ? ld_param(reinterpret_cast<const T*>(L.bias) + n) : 0.f;
-      }
       if (a.in_stats) {
         // 4 threads per token row, each summing every 4th slot in order; the
         // four partials are combined in a fixed tree order (deterministic)
@@ -599,7 +622,7 @@ struct Gemm {
     const int per_cluster = (int)cl_size() >> a.lsplit;
     const int slot = (int)cl_id() * per_cluster + ((int)cl_rank() >> a.lsplit);
     if (slot >= units || sm.pre_bytes < pre_kb_bytes(KIND)) return false;
-    prefetch(a, slot % n_tiles, sm, smem_u32(smem), pr);
+    prefetch(a, slot % n_tiles, sm, smem, pr);
     return true;
   }
 };
