@@ -12,6 +12,7 @@ CPU path.
 from __future__ import annotations
 
 import math
+import weakref
 from dataclasses import dataclass
 
 import torch
@@ -202,6 +203,10 @@ class ActionExpert(nn.Module):
         return flow_sample(self, x0, steps, self.encode(prefix))
 
 
+# plans per expert module, outside the module (so deepcopy / state_dict never see them)
+_PLANS: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+
+
 def get_plan(expert, batch: int, prefix_kv):
     """Fused-launch plan of any action-expert module (this package's or the
     reference's) for a batch and prefix K/V, cached on the module and rebuilt
@@ -209,7 +214,7 @@ def get_plan(expert, batch: int, prefix_kv):
     key = (batch, tuple(kv[0].data_ptr() for kv in prefix_kv),
            tuple((p.data_ptr(), p._version) for p in expert.parameters()),
            tuple(b.data_ptr() for b in expert.buffers()))
-    cache = expert.__dict__.setdefault("_ee_plans", {})
+    cache = _PLANS.setdefault(expert, {})
     pl = cache.get(key)
     if pl is None:
         if len(cache) > 8:

@@ -53,6 +53,59 @@ def quantize_weight_asym4(w: torch.Tensor, group_size: int = 128):
     return (q.reshape(out, inf), scale.reshape(out, -1).half(), zero.reshape(out, -1).half(), gs)
 
 
+class QuantLinear(nn.Module):
+    """kernel/quant.py:36-59: drop-in for nn.Linear holding int weights and fp32
+    scales in the reference's buffers -- ``q`` int8 [out, in/gs, gs] and
+    ``scale`` fp32 [out, in/gs, 1] -- so state dicts interchange. Where the
+    reference dequantises a full fp weight on every forward, this forward runs
+    the sm_100a dequant-GEMM on the integers directly (the kernel operands --
+    the [out, in] int8 view, or the packed int4 bytes -- are derived on first
+    use and re-derived only when ``q`` or ``scale`` changes). CUDA only."""
+
+    def __init__(self, lin: nn.Linear, bits: int, group_size: int = 128):
+        super().__init__()
+        q, scale, gs = quantize_weight(lin.weight.data.float(), bits, group_size)
+        self.register_buffer("q", q)
+        self.register_buffer("scale", scale)
+        self.gs, self.bits = gs, bits
+        self.bias = lin.bias
+        self.out_features, self.in_features = lin.weight.shape
+        self._ops = None  # (key, kernel weight, kernel scales)
+
+    def _operands(self):
+        key = (self.q.data_ptr(), self.q._version, self.scale.data_ptr(), self.scale._version)
+        if self._ops is None or self._ops[0] != key:
+            from .wq_gemm import _pack_int4
+            w2 = self.q.reshape(self.out_features, self.in_features)
+            if self.bits == 4:
+                w2 = _pack_int4(w2.contiguous())
+            self._ops = (key, w2.contiguous(), self.scale.reshape(self.out_features, -1).float().contiguous())
+        return self._ops[1], self._ops[2]
+
+    def forward(self, x):
+        from .wq_gemm import wq_linear
+        w, s = self._operands()
+        return wq_linear(x, w, s, self.bias, self.gs, self.bits)
+
+    def weight_bytes(self) -> float:
+        """kernel/quant.py:58-59: int weights plus fp16-counted scales."""
+        return self.q.numel() * self.bits / 8.0 + self.scale.numel() * 2
+
+
+def quantize_model(model: nn.Module, bits: int, group_size: int = 128,
+                   skip=("in_proj", "out_proj")) -> nn.Module:
+    """kernel/quant.py:62-73: swap the transformer linears for ``QuantLinear``
+    (IO projections stay dense); mutates and returns ``model``."""
+    for name, mod in list(model.named_children()):
+        if name in skip:
+            continue
+        if isinstance(mod, nn.Linear):
+            setattr(model, name, QuantLinear(mod, bits, group_size))
+        else:
+            quantize_model(mod, bits, group_size, skip)
+    return model
+
+
 def linear_bytes(model: nn.Module, dtype_bytes: int = 2) -> float:
     """kernel/quant.py:76-77: dense linear weight bytes at ``dtype_bytes`` each."""
     return sum(m.weight.numel() * dtype_bytes for m in model.modules() if isinstance(m, nn.Linear))
