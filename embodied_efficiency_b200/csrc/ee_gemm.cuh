@@ -25,6 +25,8 @@
 #pragma once
 
 #include "ee_common.cuh"
+#include "ee_tma.cuh"
+#include "ee_umma.cuh"
 
 namespace ee {
 
@@ -46,9 +48,12 @@ struct GemmArgs {
   int has_bias;
   int split;           // CTAs of a cluster per unit (a power of two dividing the cluster)
   int lsplit;          // log2(split)
-  // Row statistics are kept as partial (sum, sum of squares) per 16-column
-  // slice of the row: [M][stat_slots][2], summed in slot order (deterministic).
+  // Row statistics are kept as partial (sum, sum of squares) per
+  // (1 << stat_shift)-column slice of the row (16, or 8 when a unit's CTAs
+  // reduce only 8 rows): [M][stat_slots][2], summed in slot order
+  // (deterministic).
   int stat_slots;
+  int stat_shift;
   // input normalisation: when in_stats is set, every staged activation row is
   // normalised with its statistics over K and the weight / bias in_w / in_b
   // (LayerNorm) or in_w only (RMSNorm) before the MMAs
@@ -59,8 +64,12 @@ struct GemmArgs {
   float in_eps;
   // output statistics: when out_stats is set, each CTA writes the (sum, sum
   // of squares) of its output columns of every token row to the slot of its
-  // first 16 columns, and zeros to the slots of its other 16-column slices
+  // first columns, and zeros to the slots of its other column slices
   float* out_stats;       // [M][stat_slots][2]
+  // tcgen05 form: where a wait for MMA completion that runs out of time
+  // records EE_ERR_TIMEOUT, and its limit
+  int* status;
+  unsigned long long timeout_ns;
 };
 
 // Shared memory of a GEMM unit (byte offsets from the dynamic base).
@@ -71,10 +80,23 @@ struct GemmArgs {
 //   aux  norm weight/bias slice, row statistics, bias, staged scales and the
 //        residual tile of the unit
 //   pre  weight words of the first unit, copied in before a grid barrier
+//   tc   (tcgen05 form) kTcStages mbarriers (MMA completion of each A
+//        stage) at +kTcBar, the TMEM base address at +kTcTmem and the parity
+//        of every barrier's commit count (bit s) at +kTcMask; the kernel
+//        initialises it and allocates TMEM
 struct GemmSmem {
   uint32_t x, p, aux, pre;
   uint32_t pre_bytes;  // size of the pre area (0: no prefetch)
+  uint32_t tc;
 };
+// TMEM columns of the tcgen05 form: kTcStages accumulator slots of 64 fp32
+// columns (one k-block each, scaled into registers when drained), then
+// kTcStages A stages of 64 columns (128 rows x 128 k of 16-bit weights);
+// k-block kb uses slot and stage kb % kTcStages
+constexpr int kTcStages = 4;
+constexpr uint32_t kTcACol = kTcStages * 64;
+constexpr uint32_t kTcCols = 512;  // allocation: kTcStages * 128 columns
+constexpr uint32_t kTcBar = 0, kTcTmem = 8 * kTcStages, kTcMask = kTcTmem + 4, kTcStateBytes = 64;
 constexpr uint32_t kAuxGB = 0;                 // [2][2048] act: norm weight, bias slice
 constexpr uint32_t kAuxRow = 8192;             // [64][2] float: mean, rstd
 constexpr uint32_t kAuxBias = kAuxRow + 512;   // [128] float
@@ -130,9 +152,10 @@ struct PreRegs {
   int aux;  // the unit's constant operands (norm slice, scales, bias) are staged too
 };
 
-template <typename T, int KIND>
+template <typename T, int KIND, bool TC = false>
 struct Gemm {
   static constexpr int WPR = words_per_row(KIND);
+  static constexpr int CPT = 2 * WPR;  // tcgen05 form: 16-byte weight chunks per thread per k-block
 
   // k-block kb (absolute, in 128s) of row n, this thread's 32 k; n clamped to N
   static EE_DEV const char* row_ptr(const ee_linear& L, int n, int kb) {
@@ -142,14 +165,31 @@ struct Gemm {
     return reinterpret_cast<const char*>(L.weight) + (size_t)n * row_bytes +
            (size_t)kb * (kKBlock * bytes_per_k2(KIND) / 2) + t * (32 * bytes_per_k2(KIND) / 2);
   }
+  // tcgen05 form: chunk j of k-block kb for this thread, which dequantises
+  // row 32*(warp%4) + lane of the tile, k half warp/4 (64 k of the block)
+  static EE_DEV const char* tc_src(const ee_linear& L, int nt, int kb, int j) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int n = nt * kRU + 32 * (warp & 3) + lane;
+    n = n < L.n ? n : L.n - 1;
+    const size_t row_bytes = (size_t)L.k * bytes_per_k2(KIND) / 2;
+    return reinterpret_cast<const char*>(L.weight) + (size_t)n * row_bytes +
+           (size_t)kb * (kKBlock * bytes_per_k2(KIND) / 2) + (warp >> 2) * (CPT * 16) + j * 16;
+  }
+  static EE_DEV float scale_of(const ee_linear& L, int n, int kb) {
+    n = n < L.n ? n : L.n - 1;
+    const size_t si = (size_t)n * (L.k / L.group) + (kb * kKBlock) / L.group;
+    return L.scale_dtype == EE_F32 ? __ldg(reinterpret_cast<const float*>(L.scales) + si)
+                                   : __half2float(__ldg(reinterpret_cast<const __half*>(L.scales) + si));
+  }
+  static EE_DEV float zero_of(const ee_linear& L, int n, int kb) {
+    n = n < L.n ? n : L.n - 1;
+    return __half2float(__ldg(reinterpret_cast<const __half*>(L.zeros) + (size_t)n * (L.k / L.group) +
+                              (kb * kKBlock) / L.group));
+  }
   static EE_DEV void load_scales(const ee_linear& L, int n, int kb, float& s, float& z) {
     if (KIND == EE_W_DENSE) return;
-    n = n < L.n ? n : L.n - 1;
-    const int ng = L.k / L.group;
-    const size_t si = (size_t)n * ng + (kb * kKBlock) / L.group;
-    s = L.scale_dtype == EE_F32 ? __ldg(reinterpret_cast<const float*>(L.scales) + si)
-                                : __half2float(__ldg(reinterpret_cast<const __half*>(L.scales) + si));
-    if (KIND == EE_W_UINT4Z) z = __half2float(__ldg(reinterpret_cast<const __half*>(L.zeros) + si));
+    s = scale_of(L, n, kb);
+    if (KIND == EE_W_UINT4Z) z = zero_of(L, n, kb);
   }
   static EE_DEV void load_raw(const ee_linear& L, int nw, int kb, uint4 (&w)[2][WPR], float (&s)[2],
                               float (&z)[2]) {
@@ -164,6 +204,17 @@ struct Gemm {
   }
   static EE_DEV uint32_t pre_addr(uint32_t spre, int kb, int h, int i) {
     return spre + (uint32_t)((((kb * 2 + h) * WPR + i) * kThreads + threadIdx.x) * 16);
+  }
+  static EE_DEV uint32_t pre_addr_tc(uint32_t spre, int kb, int j) {
+    return spre + (uint32_t)(((kb * CPT + j) * kThreads + threadIdx.x) * 16);
+  }
+  // byte offset of logical 16-byte chunk c (8 k) of token row `row` in the
+  // staged activation slice. tcgen05 form: the K-major 128-byte-swizzled
+  // operand layout, [KS/64 slabs][64 rows][128 bytes] with the chunk index
+  // XORed with row % 8; mma.sync form: rows of KS, chunks spread by x_chunk.
+  static EE_DEV uint32_t xoff(int row, int c, int KS) {
+    if (TC) return (uint32_t)((c >> 3) * (kMTile * 128) + row * 128 + (((c & 7) ^ (row & 7)) << 4));
+    return (uint32_t)(row * KS * 2 + ((c >> 4) * 16 + x_chunk(row, c & 15)) * 16);
   }
 
   // raw words -> A-operand registers A[s][0..3] for the 8 mma steps
@@ -208,6 +259,38 @@ struct Gemm {
     }
   }
 
+  // tcgen05 form: this thread's 64 k of one weight row -> 32 packed 16-bit
+  // pairs in k order (exact integers q, or q - zero, for the quantised kinds)
+  static EE_DEV void dequant_tc(const uint4 (&w)[CPT], float z, uint32_t (&o)[32]) {
+    if (KIND == EE_W_DENSE) {
+#pragma unroll
+      for (int j = 0; j < CPT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[4 * j + e] = comp(w[j], e);
+    } else if (KIND == EE_W_INT8) {
+#pragma unroll
+      for (int j = 0; j < CPT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t wx = comp(w[j], e) ^ 0x80808080u;
+          o[8 * j + 2 * e] = int8_pair<T>(wx, 0, 1);
+          o[8 * j + 2 * e + 1] = int8_pair<T>(wx, 2, 3);
+        }
+    } else {
+      const float zoff = KIND == EE_W_INT4 ? 8.0f : z;
+      const uint32_t xor8 = KIND == EE_W_INT4 ? 0x00080008u : 0u;
+      const uint32_t nego = Act<T>::neg_offset2(Act<T>::kInt4Base + zoff);
+#pragma unroll
+      for (int j = 0; j < CPT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t ww = comp(w[j], e), w4 = ww >> 4;
+#pragma unroll
+          for (int p = 0; p < 4; ++p) o[16 * j + 4 * e + p] = fma2<T>(nib_pair<T>(ww, w4, p, xor8), Act<T>::kOne2, nego);
+        }
+    }
+  }
+
   // Start copying this CTA's first k-blocks of n-tile `nt` into the pre area
   // (one cp.async group); scales of the first k-block go to pr.
   static EE_DEV void prefetch(const GemmArgs& a, int nt, const GemmSmem& sm, char* smem, PreRegs& pr) {
@@ -216,16 +299,22 @@ struct Gemm {
     const int KB = (a.w.k >> a.lsplit) / kKBlock, kb0 = (rank & (a.split - 1)) * KB;
     const int fit = (int)(sm.pre_bytes / pre_kb_bytes(KIND));
     const int npre = KB < fit ? KB : fit;
-    const int nw = nt * kRU + 16 * (threadIdx.x >> 5), g = (threadIdx.x & 31) >> 2;
-    for (int kb = 0; kb < npre; ++kb)
+    if (TC) {
+      for (int kb = 0; kb < npre; ++kb)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const char* p = row_ptr(a.w, nw + g + 8 * h, kb0 + kb);
+        for (int j = 0; j < CPT; ++j) cp_async16(pre_addr_tc(sbase + sm.pre, kb, j), tc_src(a.w, nt, kb0 + kb, j), true);
+    } else {
+      const int nw = nt * kRU + 16 * (threadIdx.x >> 5), g = (threadIdx.x & 31) >> 2;
+      for (int kb = 0; kb < npre; ++kb)
 #pragma unroll
-        for (int i = 0; i < WPR; ++i) cp_async16(pre_addr(sbase + sm.pre, kb, h, i), p + 16 * i, true);
-      }
+        for (int h = 0; h < 2; ++h) {
+          const char* p = row_ptr(a.w, nw + g + 8 * h, kb0 + kb);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) load_scales(a.w, nw + g + 8 * h, kb0, pr.s[h], pr.z[h]);
+          for (int i = 0; i < WPR; ++i) cp_async16(pre_addr(sbase + sm.pre, kb, h, i), p + 16 * i, true);
+        }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) load_scales(a.w, nw + g + 8 * h, kb0, pr.s[h], pr.z[h]);
+    }
     stage_const(a, nt, sm, smem);
     cp_async_commit();
     pr.aux = 1;
@@ -254,9 +343,18 @@ struct Gemm {
       }
     }
     const bool smem_scales = KIND != EE_W_DENSE && L.scale_dtype == EE_F32 && KB <= kMaxKB;
-    if (smem_scales && t == 0) {
-      const int ng = L.k / L.group;
-      const float* sp = reinterpret_cast<const float*>(L.scales);
+    const int ng = L.k / L.group;
+    const float* sp = reinterpret_cast<const float*>(L.scales);
+    if (TC) {
+      // [kb][128 rows]: thread i < 128 stages row i's scales
+      if (smem_scales && threadIdx.x < kRU) {
+        int n = nt * kRU + threadIdx.x;
+        n = n < L.n ? n : L.n - 1;
+        for (int kb = 0; kb < KB; ++kb)
+          cp_async4(sbase + sm.aux + kAuxScale + (uint32_t)((kb * kRU + threadIdx.x) * 4),
+                    sp + (size_t)n * ng + ((kb0 + kb) * kKBlock) / L.group);
+      }
+    } else if (smem_scales && t == 0) {
       for (int kb = 0; kb < KB; ++kb)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -276,6 +374,103 @@ struct Gemm {
     }
   }
 
+  // tcgen05 form of the MMAs: this CTA's KB k-blocks of the 128-row tile
+  // `nt` against the staged activations (NP token rows, a multiple of 16).
+  // Per k-block the 256 threads dequantise the weights into A stage
+  // kb % kTcStages in TMEM (thread: row 32*(warp%4) + lane, k half warp/4),
+  // thread 0 issues eight 128 x NP x 16 MMAs into accumulator slot
+  // kb % kTcStages and commits them to the stage's mbarrier; a stage and slot
+  // are reused (k-block kb + kTcStages) only after those MMAs completed and
+  // the slot was drained. Slots are drained into registers with the block's
+  // fp32 scale (acc += scale * partial, in k-block order), so the arithmetic
+  // matches the mma.sync form: exact integer weights, fp32 sums, fp32 scale
+  // per k-block. Returns acc[i] = row 32*(warp%4) + lane, token
+  // 32*(warp/4) + i.
+  static EE_DEV void mma_tc(const GemmArgs& a, int nt, int kb0, int KB, int npre, int NP, uint32_t sx,
+                            char* smem, const GemmSmem& sm, float (&acc)[32]) {
+    const ee_linear& L = a.w;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, kh = warp >> 2;
+    const int row = 32 * (warp & 3) + lane, n = nt * kRU + row;
+    const uint32_t sbase = smem_u32(smem), bar = sbase + sm.tc + kTcBar;
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + sm.tc + kTcTmem);
+    uint32_t* mask_s = reinterpret_cast<uint32_t*>(smem + sm.tc + kTcMask);
+    uint32_t mask = *mask_s;  // bit s: parity of the commits issued so far to stage s's barrier
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const uint32_t idesc = umma_idesc<T>(128, NP);
+    const bool smem_scales = KIND != EE_W_DENSE && L.scale_dtype == EE_F32 && KB <= kMaxKB;
+    const float* ssc = reinterpret_cast<const float*>(smem + sm.aux + kAuxScale);
+    const bool tok_live = 32 * kh < NP;  // warp-uniform
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+
+    auto wait_stage = [&](int s) {  // the last commit to stage s has completed
+      if (!mbar_wait(bar + 8 * s, ((mask >> s) & 1u) ^ 1u, a.timeout_ns)) ok = false;
+    };
+    auto drain = [&](int kbd) {  // slot of k-block kbd -> acc (its MMAs have completed)
+      if (!tok_live) return;
+      uint32_t v[32];
+      tmem_ld32(tmem + lane_off + (uint32_t)(64 * (kbd % kTcStages) + 32 * kh), v);
+      tmem_wait_ld();
+      const float sc = KIND == EE_W_DENSE ? 1.f : (smem_scales ? ssc[kbd * kRU + row] : scale_of(L, n, kb0 + kbd));
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] = fmaf(sc, __uint_as_float(v[i]), acc[i]);
+    };
+    auto fetch = [&](int kb, uint4 (&w)[CPT]) {
+      if (kb < npre) {
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) w[j] = lds16(pre_addr_tc(sbase + sm.pre, kb, j));
+      } else {
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) w[j] = ld_weight16(tc_src(L, nt, kb0 + kb, j));
+      }
+    };
+
+    auto issue = [&](int kb) {  // thread 0: the eight MMAs of k-block kb, committed to its stage
+      const int s = kb % kTcStages;
+      const uint32_t d = tmem + (uint32_t)(64 * s);
+      const uint32_t at = tmem + kTcACol + (uint32_t)(64 * s);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_f16_ts(d, at + 8 * ks, umma_desc_sw128(sx + (uint32_t)((2 * kb + (ks >> 2)) * (kMTile * 128) + (ks & 3) * 32)),
+                    idesc, ks > 0 ? 1u : 0u);
+      umma_commit(bar + 8 * s);
+    };
+
+    uint4 raw[CPT];
+    fetch(0, raw);
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % kTcStages;
+      uint4 cur[CPT];
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) cur[j] = raw[j];
+      if (kb + 1 < KB) fetch(kb + 1, raw);
+      const float z = KIND == EE_W_UINT4Z ? zero_of(L, n, kb0 + kb) : 0.f;
+      if (kb >= kTcStages) {
+        wait_stage(s);  // k-block kb - kTcStages (stage s, slot s) is done
+        tc_fence_after();
+        drain(kb - kTcStages);
+      }
+      uint32_t o[32];
+      dequant_tc(cur, z, o);
+      tmem_st32(tmem + lane_off + kTcACol + (uint32_t)(64 * s + 32 * kh), o);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        tc_fence_after();
+        issue(kb);
+      }
+      mask ^= 1u << s;
+    }
+    // every MMA of the unit has completed once each used stage's last commit has
+    for (int s = 0; s < kTcStages && s < KB; ++s) wait_stage(s);
+    tc_fence_after();
+    for (int kbd = KB > kTcStages ? KB - kTcStages : 0; kbd < KB; ++kbd) drain(kbd);
+    if (!ok && threadIdx.x == 0 && a.status) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
+    if (threadIdx.x == 0) *mask_s = mask;
+  }
+
   // One unit: rows nt*128 .. +127 x tokens m0 .. m0+63 over all of K, by the S
   // CTAs of sub-cluster rank/S. Every CTA of the cluster calls this the same
   // number of times (inactive CTAs only join the cluster barriers).
@@ -289,6 +484,8 @@ struct Gemm {
     const int RPR = kRU >> a.lsplit;  // rows this CTA reduces and stores
     const int mrows = active ? min(kMTile, a.M - m0) : 0;
     const int JT = (mrows + 7) >> 3;
+    // token rows the MMAs read (tcgen05 N: a multiple of 16; rows past mrows are zero)
+    const int NP = TC ? ((mrows + 15) & ~15) : JT * 8;
     const int nw = nt * kRU + 16 * warp;
     const int nbase = nt * kRU + r * RPR;
     const uint32_t sbase = smem_u32(smem);
@@ -297,12 +494,6 @@ struct Gemm {
     float* rowst = reinterpret_cast<float*>(aux + kAuxRow);
     float* sbias = reinterpret_cast<float*>(aux + kAuxBias);
     T* sres = reinterpret_cast<T*>(aux + kAuxRes);
-
-    float acc[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[j][c] = 0.f;
 
     // weights: prefetched before the grid barrier, or requested now
     PreRegs pr_local;
@@ -313,9 +504,6 @@ struct Gemm {
     }
     const int fit = (int)(sm.pre_bytes / pre_kb_bytes(KIND));
     const int npre = prw ? (KB < fit ? KB : fit) : 0;
-    // fp32 scales of every k-block are staged in shared memory
-    const bool smem_scales = KIND != EE_W_DENSE && L.scale_dtype == EE_F32 && KB <= kMaxKB;
-    float* ssc = reinterpret_cast<float*>(aux + kAuxScale);  // [kb][h][warp][g]
 
     if (active) {
       // 1. activation slice, norm weight / bias slice, residual tile -> smem
@@ -326,17 +514,16 @@ struct Gemm {
         const int c = threadIdx.x % cpr, rstep = kThreads / cpr;
         const char* src = xb + ((size_t)m0 * a.ldx + (size_t)kb0 * kKBlock + c * 8) * 2;
         const size_t sstep = (size_t)a.ldx * 2;
-        for (int row = threadIdx.x / cpr; row < JT * 8; row += rstep) {
+        for (int row = threadIdx.x / cpr; row < NP; row += rstep) {
           const bool ok = row < mrows;
-          cp_async16(sx + (uint32_t)(row * KS * 2 + ((c >> 4) * 16 + x_chunk(row, c & 15)) * 16),
-                     ok ? src + (size_t)row * sstep : src, ok);
+          cp_async16(sx + xoff(row, c, KS), ok ? src + (size_t)row * sstep : src, ok);
         }
       } else {
-        for (int i = threadIdx.x; i < JT * 8 * cpr; i += kThreads) {
+        for (int i = threadIdx.x; i < NP * cpr; i += kThreads) {
           const int row = i / cpr, c = i - row * cpr;
           const bool ok = row < mrows;
           const char* src = xb + ((size_t)(m0 + (ok ? row : 0)) * a.ldx + (size_t)kb0 * kKBlock + c * 8) * 2;
-          cp_async16(sx + (uint32_t)(row * KS * 2 + ((c >> 4) * 16 + x_chunk(row, c & 15)) * 16), src, ok);
+          cp_async16(sx + xoff(row, c, KS), src, ok);
         }
       }
       if (!(prw && prw->aux)) stage_const(a, nt, sm, smem);  // else staged before the barrier
@@ -389,115 +576,140 @@ struct Gemm {
         }
       }
     }
-    // 2. weights of the first k-block (from the pre area, or loaded now)
+    // 2. weights of the first k-block (mma.sync form: from the pre area, or loaded now)
     uint4 w[2][WPR];
     float sc[2] = {1.f, 1.f}, zr[2] = {0.f, 0.f};
     if (active) {
       cp_async_wait<0>();
-      if (prw) {
+      if (!TC) {
+        if (prw) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+          for (int h = 0; h < 2; ++h) {
 #pragma unroll
-          for (int i = 0; i < WPR; ++i) w[h][i] = lds16(pre_addr(sbase + sm.pre, 0, h, i));
-          sc[h] = prw->s[h];
-          zr[h] = prw->z[h];
+            for (int i = 0; i < WPR; ++i) w[h][i] = lds16(pre_addr(sbase + sm.pre, 0, h, i));
+            sc[h] = prw->s[h];
+            zr[h] = prw->z[h];
+          }
+        } else {
+          load_raw(L, nw, kb0, w, sc, zr);
         }
-      } else {
-        load_raw(L, nw, kb0, w, sc, zr);
       }
     }
     __syncthreads();
 
+    float acc[8][4];  // mma.sync form: token tile j, fragment c
+    float acct[32];   // tcgen05 form: row 32*(warp%4)+lane, tokens 32*(warp/4)+i
     if (active) {
       // 3. normalise the staged activations in place
       if (a.in_stats) {
         const int cpr = KS / 8;
         const T* sgw = reinterpret_cast<const T*>(aux + kAuxGB);
         const T* sgb = sgw + kMaxNormSlice;
-        const bool fixed_col = (kThreads % cpr) == 0;  // thread keeps one chunk column
-        const int rstep = fixed_col ? kThreads / cpr : 0;
-        for (int i = threadIdx.x, row = fixed_col ? threadIdx.x / cpr : 0, pc = fixed_col ? threadIdx.x % cpr : 0;
-             fixed_col ? row < mrows : i < mrows * cpr; i += kThreads, row += rstep) {
-          if (!fixed_col) {
-            row = i / cpr;
-            pc = i - row * cpr;
-          }
-          const int c = (pc & ~15) + x_chunk(row, pc & 15);  // logical chunk of physical pc
-          uint4* q = reinterpret_cast<uint4*>(smem + sm.x + row * KS * 2 + pc * 16);
+        const bool rms = a.in_norm == EE_NORM_RMS;
+        auto norm_chunk = [&](int row, int c, const float2 (&wf)[4], const float2 (&bf)[4]) {
+          uint4* q = reinterpret_cast<uint4*>(smem + sm.x + xoff(row, c, KS));
           const uint4 v = *q;
-          const uint4 wv = *reinterpret_cast<const uint4*>(sgw + c * 8);
-          const uint4 bv = *reinterpret_cast<const uint4*>(sgb + c * 8);
           const float mean = rowst[2 * row], rstd = rowst[2 * row + 1];
           uint32_t o[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 xv = Act<T>::unpack2(comp(v, e));
-            const float2 wf = Act<T>::unpack2(comp(wv, e));
-            if (a.in_norm == EE_NORM_RMS) {
-              o[e] = Act<T>::pack2(Act<T>::round(xv.x * rstd) * wf.x, Act<T>::round(xv.y * rstd) * wf.y);
+            if (rms) {
+              o[e] = Act<T>::pack2(Act<T>::round(xv.x * rstd) * wf[e].x, Act<T>::round(xv.y * rstd) * wf[e].y);
             } else {
-              const float2 bf = Act<T>::unpack2(comp(bv, e));
-              o[e] = Act<T>::pack2((xv.x - mean) * rstd * wf.x + bf.x, (xv.y - mean) * rstd * wf.y + bf.y);
+              o[e] = Act<T>::pack2((xv.x - mean) * rstd * wf[e].x + bf[e].x, (xv.y - mean) * rstd * wf[e].y + bf[e].y);
             }
           }
           *q = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-        __syncthreads();
-      }
-
-      // 4. MMAs over this CTA's k-blocks (first pre_kb from the pre area)
-      for (int kb = 0; kb < KB; ++kb) {
-        uint32_t A[8][4];
-        dequant(w, zr, A);
-        const float s0 = sc[0], s1 = sc[1];
-        if (kb + 1 < KB) {
-          if (kb + 1 < npre) {
+        };
+        auto load_wb = [&](int c, float2 (&wf)[4], float2 (&bf)[4]) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(sgw + c * 8);
+          const uint4 bv = *reinterpret_cast<const uint4*>(sgb + c * 8);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-#pragma unroll
-              for (int i = 0; i < WPR; ++i) w[h][i] = lds16(pre_addr(sbase + sm.pre, kb + 1, h, i));
-              if (smem_scales) {
-                sc[h] = ssc[(((kb + 1) * 2 + h) * kWarps + warp) * 8 + g];
-                if (KIND == EE_W_UINT4Z)
-                  zr[h] = __half2float(__ldg(reinterpret_cast<const __half*>(L.zeros) +
-                                             (size_t)min(nw + g + 8 * h, L.n - 1) * (L.k / L.group) +
-                                             ((kb0 + kb + 1) * kKBlock) / L.group));
-              } else {
-                load_scales(L, nw + g + 8 * h, kb0 + kb + 1, sc[h], zr[h]);
-              }
-            }
-          } else {
-            load_raw(L, nw, kb0 + kb + 1, w, sc, zr);
+          for (int e = 0; e < 4; ++e) {
+            wf[e] = Act<T>::unpack2(comp(wv, e));
+            bf[e] = Act<T>::unpack2(comp(bv, e));
+          }
+        };
+        if (kThreads % cpr == 0) {
+          // one chunk column per thread: its norm weight / bias loaded once
+          const int c = threadIdx.x % cpr, rstep = kThreads / cpr;
+          float2 wf[4], bf[4];
+          load_wb(c, wf, bf);
+#pragma unroll 4
+          for (int row = threadIdx.x / cpr; row < mrows; row += rstep) norm_chunk(row, c, wf, bf);
+        } else {
+          for (int i = threadIdx.x; i < mrows * cpr; i += kThreads) {
+            const int row = i / cpr, c = i - row * cpr;
+            float2 wf[4], bf[4];
+            load_wb(c, wf, bf);
+            norm_chunk(row, c, wf, bf);
           }
         }
+        if (!TC) __syncthreads();  // the tcgen05 form syncs before its first MMA
+      }
+
+      if (TC) {
+        // 4. tcgen05 MMAs (activations written by this thread -> async proxy first)
+        fence_proxy_async_smem();
+        mma_tc(a, nt, kb0, KB, npre, NP, sx, smem, sm, acct);
+      } else {
+        // 4. mma.sync MMAs over this CTA's k-blocks (first pre_kb from the pre area)
+        const bool smem_scales = KIND != EE_W_DENSE && L.scale_dtype == EE_F32 && KB <= kMaxKB;
+        const float* ssc = reinterpret_cast<const float*>(aux + kAuxScale);  // [kb][h][warp][g]
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (j < JT) {
-            const int row = 8 * j + g;
-            const uint32_t rbase = sx + (uint32_t)(row * KS * 2 + kb * 256);
-            uint4 xq[4];
+        for (int j = 0; j < 8; ++j)
 #pragma unroll
-            for (int s2 = 0; s2 < 4; ++s2) xq[s2] = lds16(rbase + x_chunk(row, 4 * t + s2) * 16);
-            // four independent accumulation chains of two MMAs each (chain c
-            // takes steps 2c and 2c+1, i.e. the k of xq[c]), so an MMA's
-            // latency is exposed twice per token tile, not eight times
-            float pc[4][4];
+          for (int c = 0; c < 4; ++c) acc[j][c] = 0.f;
+        for (int kb = 0; kb < KB; ++kb) {
+          uint32_t A[8][4];
+          dequant(w, zr, A);
+          const float s0 = sc[0], s1 = sc[1];
+          if (kb + 1 < KB) {
+            if (kb + 1 < npre) {
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc)
+              for (int h = 0; h < 2; ++h) {
 #pragma unroll
-              for (int e = 0; e < 4; ++e) pc[cc][e] = 0.f;
-#pragma unroll
-            for (int hs = 0; hs < 2; ++hs)
-#pragma unroll
-              for (int cc = 0; cc < 4; ++cc) {
-                const int s = 2 * cc + hs;
-                mma16816<T>(pc[cc], A[s][0], A[s][1], A[s][2], A[s][3], comp(xq[cc], 2 * hs), comp(xq[cc], 2 * hs + 1));
+                for (int i = 0; i < WPR; ++i) w[h][i] = lds16(pre_addr(sbase + sm.pre, kb + 1, h, i));
+                if (smem_scales) {
+                  sc[h] = ssc[(((kb + 1) * 2 + h) * kWarps + warp) * 8 + g];
+                  if (KIND == EE_W_UINT4Z) zr[h] = zero_of(L, nw + g + 8 * h, kb0 + kb + 1);
+                } else {
+                  load_scales(L, nw + g + 8 * h, kb0 + kb + 1, sc[h], zr[h]);
+                }
               }
-            const float f0 = KIND == EE_W_DENSE ? 1.f : s0, f1 = KIND == EE_W_DENSE ? 1.f : s1;
-            acc[j][0] += f0 * ((pc[0][0] + pc[1][0]) + (pc[2][0] + pc[3][0]));
-            acc[j][1] += f0 * ((pc[0][1] + pc[1][1]) + (pc[2][1] + pc[3][1]));
-            acc[j][2] += f1 * ((pc[0][2] + pc[1][2]) + (pc[2][2] + pc[3][2]));
-            acc[j][3] += f1 * ((pc[0][3] + pc[1][3]) + (pc[2][3] + pc[3][3]));
+            } else {
+              load_raw(L, nw, kb0 + kb + 1, w, sc, zr);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (j < JT) {
+              const int row = 8 * j + g;
+              uint4 xq[4];
+#pragma unroll
+              for (int s2 = 0; s2 < 4; ++s2) xq[s2] = lds16(sx + xoff(row, kb * 16 + 4 * t + s2, KS));
+              // four independent accumulation chains of two MMAs each (chain c
+              // takes steps 2c and 2c+1, i.e. the k of xq[c]), so an MMA's
+              // latency is exposed twice per token tile, not eight times
+              float pc[4][4];
+#pragma unroll
+              for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) pc[cc][e] = 0.f;
+#pragma unroll
+              for (int hs = 0; hs < 2; ++hs)
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                  const int s = 2 * cc + hs;
+                  mma16816<T>(pc[cc], A[s][0], A[s][1], A[s][2], A[s][3], comp(xq[cc], 2 * hs), comp(xq[cc], 2 * hs + 1));
+                }
+              const float f0 = KIND == EE_W_DENSE ? 1.f : s0, f1 = KIND == EE_W_DENSE ? 1.f : s1;
+              acc[j][0] += f0 * ((pc[0][0] + pc[1][0]) + (pc[2][0] + pc[3][0]));
+              acc[j][1] += f0 * ((pc[0][1] + pc[1][1]) + (pc[2][1] + pc[3][1]));
+              acc[j][2] += f1 * ((pc[0][2] + pc[1][2]) + (pc[2][2] + pc[3][2]));
+              acc[j][3] += f1 * ((pc[0][3] + pc[1][3]) + (pc[2][3] + pc[3][3]));
+            }
           }
         }
       }
@@ -505,18 +717,28 @@ struct Gemm {
       // 5. push the partial tile: rows of rank q go to rank q's receive buffer
       const uint32_t rbuf = sbase + sm.p + (uint32_t)(parity * kPBytes);
       const int rshift = 7 - a.lsplit;  // log2(RPR)
+      if (TC) {
+        const int row = 32 * (warp & 3) + lane, t0 = 32 * (warp >> 2);
+        const int owner = row >> rshift, lrow = row & (RPR - 1);
+        const uint32_t dst = mapa(rbuf + (uint32_t)(((r * RPR + lrow) * kPS + t0) * 4), (uint32_t)(sub0 + owner));
+        const int nq = t0 < mrows ? (min(32, mrows - t0) + 3) >> 2 : 0;  // 4-token groups to send
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (j < JT) {
-          const int c0 = 8 * j + 2 * t;
+        for (int q = 0; q < 8; ++q)
+          if (q < nq) st_dsmem_f4(dst + 16 * q, acct[4 * q], acct[4 * q + 1], acct[4 * q + 2], acct[4 * q + 3]);
+      } else {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int row = 16 * warp + g + 8 * h;
-            const int owner = row >> rshift, lrow = row & (RPR - 1);
-            const uint32_t off = (uint32_t)(((r * RPR + lrow) * kPS + c0) * 4);
-            st_dsmem_f2(mapa(rbuf + off, (uint32_t)(sub0 + owner)), acc[j][2 * h], acc[j][2 * h + 1]);
+        for (int j = 0; j < 8; ++j)
+          if (j < JT) {
+            const int c0 = 8 * j + 2 * t;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int row = 16 * warp + g + 8 * h;
+              const int owner = row >> rshift, lrow = row & (RPR - 1);
+              const uint32_t off = (uint32_t)(((r * RPR + lrow) * kPS + c0) * 4);
+              st_dsmem_f2(mapa(rbuf + off, (uint32_t)(sub0 + owner)), acc[j][2 * h], acc[j][2 * h + 1]);
+            }
           }
-        }
+      }
     }
     cluster_sync();  // every partial of this round has arrived
 
@@ -525,9 +747,10 @@ struct Gemm {
     float* E = reinterpret_cast<float*>(smem + sm.x);  // [64][ES], reuses the X slice
     if (active) {
       const float* R = reinterpret_cast<const float*>(smem + sm.p + parity * kPBytes);
+      const int nc4 = (mrows + 3) >> 2;  // 4-token groups holding real tokens
       for (int i = threadIdx.x; i < RPR * 16; i += kThreads) {
         const int row = i >> 4, c4 = i & 15;
-        if (4 * c4 < JT * 8) {
+        if (c4 < nc4) {
           float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
           for (int q = 0; q < S; ++q) {
             const float4 v = *reinterpret_cast<const float4*>(R + (q * RPR + row) * kPS + 4 * c4);
@@ -584,10 +807,10 @@ struct Gemm {
             sx += y;
             sxx += y * y;
           }
-          float* st = a.out_stats + 2 * ((size_t)(m0 + threadIdx.x) * a.stat_slots + (nbase >> 4));
+          float* st = a.out_stats + 2 * ((size_t)(m0 + threadIdx.x) * a.stat_slots + (nbase >> a.stat_shift));
           st[0] = sx;
           st[1] = sxx;
-          for (int q = 1; q < (RPR >> 4); ++q) {
+          for (int q = 1; q < (RPR >> a.stat_shift); ++q) {
             st[2 * q] = 0.f;
             st[2 * q + 1] = 0.f;
           }

@@ -63,7 +63,7 @@ static int launch_gemm_k(GemmArgs a, cudaStream_t s) {
   const size_t e = (size_t)rows8 * (kRU / cl + 1) * 4;
   if (e > x) x = e;
   x = (x + 127) & ~(size_t)127;
-  GemmSmem sm;
+  GemmSmem sm{};
   sm.x = 0;
   sm.p = (uint32_t)x;
   sm.aux = (uint32_t)(x + 2 * kPBytes);

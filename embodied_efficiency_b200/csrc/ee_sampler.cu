@@ -114,6 +114,8 @@ int ee_flow_sample_geometry(const ee_expert* exp, int32_t* grid_ctas, int32_t* c
   if (rc) return rc;
   Ctx c{};
   c.ex = *exp;
+  c.M = c.ex.batch * c.ex.horizon;
+  c.Rt = c.ex.batch;
   c.ks_cap = sampler_ks_cap(c.ex);
   {
     const SamplerSmem sm = sampler_smem_map(c.ex, device_props()->smem_optin);

@@ -50,7 +50,8 @@ struct Ctx {
   float* stats;  // [2][M][n_slots][2] row (sum, sum of squares) of the norm inputs,
                  // alternating between the two halves by norm sequence number
   int n_inst;    // norms per step (3 per block, 2 without self-attention)
-  int n_slots;   // partial-statistics slots per row: 16-column slices of d
+  int n_slots;   // partial-statistics slots per row: (1 << stat_shift)-column slices of d
+  int stat_shift;
   uint32_t desc; // shared-memory copy of the block table (byte offset)
   int ks_cap;    // largest K slice a GEMM unit may stage
   int lsplit[7]; // log2 CTAs per unit of t_proj, qkv, proj, q_c, out_c, mlp0, mlp2
@@ -104,6 +105,7 @@ EE_DEV GemmArgs make_gemm(const Ctx& c, const Phase& ph, const char* smem) {
   const int d = c.ex.d_model;
   a.M = c.M;
   a.stat_slots = c.n_slots;
+  a.stat_shift = c.stat_shift;
   a.in_norm = c.ex.norm_kind;
   a.in_eps = c.ex.eps;
   if (ph.type == PH_TPROJ) {
@@ -146,6 +148,8 @@ EE_DEV GemmArgs make_gemm(const Ctx& c, const Phase& ph, const char* smem) {
     if (a.epi == EPI_RESID) { a.resid = c.x; a.ldr = d; }
   }
   a.has_bias = a.w.bias != nullptr;
+  a.status = c.status;
+  a.timeout_ns = c.timeout_ns;
   const int gi = ph.type == PH_TPROJ ? 0 : (ph.sub == 0 ? 1 : ph.sub == 2 ? 2 : ph.sub == 3 ? 3 : ph.sub == 5 ? 4 : ph.sub == 6 ? 5 : 6);
   a.lsplit = c.lsplit[gi];
   a.split = 1 << a.lsplit;
@@ -159,20 +163,20 @@ EE_DEV bool gemm_dispatch(const GemmArgs& a, char* smem, const GemmSmem& sm, con
                           bool prefetch, PreRegs* pr_out) {
   switch (a.w.wkind) {
     case EE_W_DENSE:
-      if (prefetch) return Gemm<T, EE_W_DENSE>::start_prefetch(a, sm, smem, *pr_out);
-      Gemm<T, EE_W_DENSE>::run(a, smem, sm, pre);
+      if (prefetch) return Gemm<T, EE_W_DENSE, true>::start_prefetch(a, sm, smem, *pr_out);
+      Gemm<T, EE_W_DENSE, true>::run(a, smem, sm, pre);
       break;
     case EE_W_INT8:
-      if (prefetch) return Gemm<T, EE_W_INT8>::start_prefetch(a, sm, smem, *pr_out);
-      Gemm<T, EE_W_INT8>::run(a, smem, sm, pre);
+      if (prefetch) return Gemm<T, EE_W_INT8, true>::start_prefetch(a, sm, smem, *pr_out);
+      Gemm<T, EE_W_INT8, true>::run(a, smem, sm, pre);
       break;
     case EE_W_INT4:
-      if (prefetch) return Gemm<T, EE_W_INT4>::start_prefetch(a, sm, smem, *pr_out);
-      Gemm<T, EE_W_INT4>::run(a, smem, sm, pre);
+      if (prefetch) return Gemm<T, EE_W_INT4, true>::start_prefetch(a, sm, smem, *pr_out);
+      Gemm<T, EE_W_INT4, true>::run(a, smem, sm, pre);
       break;
     default:
-      if (prefetch) return Gemm<T, EE_W_UINT4Z>::start_prefetch(a, sm, smem, *pr_out);
-      Gemm<T, EE_W_UINT4Z>::run(a, smem, sm, pre);
+      if (prefetch) return Gemm<T, EE_W_UINT4Z, true>::start_prefetch(a, sm, smem, *pr_out);
+      Gemm<T, EE_W_UINT4Z, true>::run(a, smem, sm, pre);
   }
   return false;
 }
@@ -445,7 +449,8 @@ EE_DEV bool grid_wait(const Ctx& c, unsigned target) {
 
 template <typename T, int HD>
 __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_constant__ Ctx c) {
-  extern __shared__ __align__(128) char smem[];
+  extern __shared__ __align__(128) char smem_raw[];
+  char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   PreRegs pre;
   bool have_pre = false;
   const int P = num_phases(c);
@@ -462,8 +467,30 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
     unsigned long long* dst = reinterpret_cast<unsigned long long*>(smem + c.desc);
     const int n = c.ex.n_layers * (int)(sizeof(ee_block) / 8);
     for (int i = threadIdx.x; i < n; i += kThreads) dst[i] = src[i];
-    __syncthreads();
   }
+  // tcgen05 state: the two stage mbarriers and the TMEM columns the GEMM
+  // units use for the whole call (one CTA per SM, so the allocation is free)
+  const uint32_t tc_state = smem_u32(smem) + c.sm.tc;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) mbar_init(tc_state + kTcBar + 8 * s, 1);
+    *reinterpret_cast<uint32_t*>(smem + c.sm.tc + kTcMask) = 0;
+    mbar_fence_init();
+  }
+  if (threadIdx.x < 32) {
+    tmem_alloc(tc_state + kTcTmem, kTcCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  auto release_tmem = [&]() {  // every tcgen05 operation of this CTA has completed
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      tc_fence_after();
+      tmem_dealloc(*reinterpret_cast<volatile uint32_t*>(smem + c.sm.tc + kTcTmem), kTcCols);
+    }
+  };
 
   for (int p = 0; p < P; ++p) {
     const Phase ph = decode(c, p);
@@ -545,12 +572,14 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
         have_pre = gemm_dispatch<T>(make_gemm(c, nx, smem), smem, c.sm, nullptr, true, &pre);
       if (!grid_wait(c, target)) {
         cp_async_wait<0>();
+        release_tmem();
         return;
       }
     }
     if (c.trace && threadIdx.x == 0)
       c.trace[((size_t)p * gridDim.x + blockIdx.x) * 2 + 1] = globaltimer();
   }
+  release_tmem();
 }
 
 // ---------------------------------------------------------------------------
@@ -572,7 +601,7 @@ inline Layout layout_for(const ee_expert& ex, int n_steps) {
   L.Rt_max = n_steps * ex.batch;
   size_t off = 0;
   L.sync = off; off += 256;
-  L.n_slots = (ex.d_model + 15) / 16;
+  L.n_slots = (ex.d_model + 7) / 8;  // room for 8-column slots
   L.stats = off; off += al256((size_t)2 * L.M * L.n_slots * 2 * sizeof(float));
   L.x = off; off += al256((size_t)L.M * d * e);
   L.qkv = off; off += ex.self_attn ? al256((size_t)L.M * 3 * d * e) : 0;
@@ -585,8 +614,10 @@ inline Layout layout_for(const ee_expert& ex, int n_steps) {
   return L;
 }
 
-// cluster size of the sampler: the model width must split into 128-wide
-// k-blocks across the cluster (K = d_model is the smallest GEMM K)
+// portable cluster size of the sampler: the model width must split into
+// 128-wide k-blocks across the cluster (K = d_model is the smallest GEMM K).
+// Where it is 8, a cluster of 16 (non-portable; units of K = d_model then
+// take half a cluster) is also considered.
 inline int sampler_cluster(const ee_expert& ex) {
   const int kb = ex.d_model / 128;
   int cl = 8;
@@ -625,11 +656,15 @@ inline SamplerSmem sampler_smem_map(const ee_expert& ex, int smem_optin) {
   if (desc < attn) desc = attn;
   desc = (desc + 127) & ~(size_t)127;
   sm.desc = (uint32_t)desc;
-  const size_t pre = (desc + (size_t)ex.n_layers * sizeof(ee_block) + 127) & ~(size_t)127;
+  // tcgen05 state (mbarriers, TMEM address, commit counts) after the block table
+  sm.g.tc = (uint32_t)((desc + (size_t)ex.n_layers * sizeof(ee_block) + 15) & ~(size_t)15);
+  const size_t pre = (sm.g.tc + kTcStateBytes + 127) & ~(size_t)127;
   sm.g.pre = (uint32_t)pre;
-  const long long room = (long long)smem_optin - 1024 - (long long)pre;  // 1 KB static reserve
+  // 1 KB static reserve, 1 KB to align the dynamic base to 1024 bytes (the
+  // 128-byte-swizzled operand tiles start on 1024-byte boundaries)
+  const long long room = (long long)smem_optin - 2048 - (long long)pre;
   sm.g.pre_bytes = room > 0 ? (uint32_t)(room < 128 * 1024 ? room : 128 * 1024) : 0;
-  sm.total = pre + sm.g.pre_bytes;
+  sm.total = pre + sm.g.pre_bytes + 1024;
   return sm;
 }
 
@@ -661,7 +696,7 @@ inline int validate_expert(const ee_expert& ex, int n_steps, int mode) {
     return EE_ERR_ALIGN;
   // shared memory must hold the widest GEMM slice next to the fixed regions
   const SamplerSmem sm = sampler_smem_map(ex, 232448);
-  if ((size_t)sm.g.pre + 1024 > 232448) return EE_ERR_UNSUPPORTED;
+  if ((size_t)sm.g.pre + 2048 > 232448) return EE_ERR_UNSUPPORTED;
   return validate_linear(ex.t_proj, ex.d_model, ex.d_model);
 }
 
@@ -695,66 +730,132 @@ constexpr auto fn_of() { return sampler_kernel<T, HD>; }
 
 // Launch geometry of the sampler kernel: clusters of `cl` CTAs, as many as
 // can be resident at once (at most one CTA per SM).
+// GEMM shapes of a step (n, k, tokens): t_proj, qkv, proj, q_c, out_c, mlp0, mlp2
+inline void step_shapes(const Ctx& c, int (&shapes)[7][3]) {
+  const ee_expert& ex = c.ex;
+  const int d = ex.d_model, M = c.M;
+  const int sh[7][3] = {{d, d, c.Rt}, {3 * d, d, M}, {d, d, M}, {d, d, M},
+                        {d, d, M}, {ex.hidden, d, M}, {d, ex.hidden, M}};
+  for (int i = 0; i < 7; ++i)
+    for (int j = 0; j < 3; ++j) shapes[i][j] = sh[i][j];
+}
+
+// Serial work of a CTA over one step's GEMMs with `grid` CTAs in clusters of
+// `cl`: sum of rounds x k-blocks per unit under pick_split (-1: no split fits).
+inline long long plan_cost(const Ctx& c, int grid, int cl) {
+  int shapes[7][3];
+  step_shapes(c, shapes);
+  long long cost = 0;
+  for (int i = 1; i < 7; ++i) {
+    const int sp = pick_split(shapes[i][0], shapes[i][1], shapes[i][2], grid / cl, cl, c.ks_cap);
+    if (sp <= 0) return -1;
+    const long long units = (long long)((shapes[i][0] + kRU - 1) / kRU) * ((shapes[i][2] + kMTile - 1) / kMTile);
+    const long long slots = (long long)(grid / cl) * (cl / sp);
+    cost += ((units + slots - 1) / slots) * (shapes[i][1] / sp / kKBlock);
+  }
+  return cost;
+}
+
+// Launch geometry of the sampler kernel: clusters of `cl` CTAs, as many as
+// can be resident at once (at most one CTA per SM); of the candidate cluster
+// sizes the one whose GEMM plan has the least serial work per CTA (ties: the
+// portable size).
 template <typename T, int HD>
 int sampler_geometry(const Ctx& c, int* grid, int* cl_out, size_t* smem_out) {
   auto fn = sampler_kernel<T, HD>;
-  const int cl = sampler_cluster(c.ex);
+  const int cl0 = sampler_cluster(c.ex);
   const size_t smem = c.smem_bytes;
   static std::atomic<int> smem_set[64];
   allow_max_smem(fn, smem_set);
-  // the occupancy query is costly: remember the last answer per device
+  const int cands[2] = {cl0, cl0 == 8 ? 16 : 0};
+  // the occupancy queries are costly: remember the resident grid of each
+  // candidate per device (0: the candidate cannot launch)
   static std::mutex mu;
-  static struct { int cl; size_t smem; int grid; } memo[64] = {};
+  static struct { int cl0; size_t smem; int grids[2]; bool valid; } memo[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return EE_ERR_DEVICE;
+  int grids[2] = {0, 0};
+  bool have = false;
   {
     std::lock_guard<std::mutex> g(mu);
-    if (memo[dev].grid > 0 && memo[dev].cl == cl && memo[dev].smem == smem) {
-      *grid = memo[dev].grid;
-      *cl_out = cl;
-      *smem_out = smem;
-      return EE_OK;
+    if (memo[dev].valid && memo[dev].cl0 == cl0 && memo[dev].smem == smem) {
+      grids[0] = memo[dev].grids[0];
+      grids[1] = memo[dev].grids[1];
+      have = true;
     }
   }
-  cudaLaunchConfig_t cfg{};
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cl;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cfg.gridDim = dim3(cl);
-  int nclusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&nclusters, fn, &cfg) != cudaSuccess || nclusters < 1)
-    return EE_ERR_LAUNCH;
-  const int max_ctas = device_sms();
-  if (nclusters * cl > max_ctas) nclusters = max_ctas / cl;
-  *grid = nclusters * cl;
-  *cl_out = cl;
+  if (!have) {
+    const int max_ctas = device_sms();
+    for (int ci = 0; ci < 2; ++ci) {
+      const int cl = cands[ci];
+      if (cl <= 0) continue;
+      if (cl > 8 && cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        cudaGetLastError();
+        continue;
+      }
+      cudaLaunchConfig_t cfg{};
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = cl;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      cfg.gridDim = dim3(cl);
+      int nclusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&nclusters, fn, &cfg) != cudaSuccess || nclusters < 1) {
+        cudaGetLastError();
+        continue;
+      }
+      if (nclusters * cl > max_ctas) nclusters = max_ctas / cl;
+      grids[ci] = nclusters * cl;
+    }
+    std::lock_guard<std::mutex> g(mu);
+    memo[dev].cl0 = cl0;
+    memo[dev].smem = smem;
+    memo[dev].grids[0] = grids[0];
+    memo[dev].grids[1] = grids[1];
+    memo[dev].valid = true;
+  }
+  int best_grid = 0, best_cl = 0;
+  long long best_cost = -1;
+  for (int ci = 0; ci < 2; ++ci) {
+    if (grids[ci] <= 0) continue;
+    const long long cost = plan_cost(c, grids[ci], cands[ci]);
+    if (cost < 0) continue;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_grid = grids[ci];
+      best_cl = cands[ci];
+    }
+  }
+  if (best_grid <= 0) return EE_ERR_LAUNCH;
+  *grid = best_grid;
+  *cl_out = best_cl;
   *smem_out = smem;
-  std::lock_guard<std::mutex> g(mu);
-  memo[dev].cl = cl;
-  memo[dev].smem = smem;
-  memo[dev].grid = *grid;
   return EE_OK;
 }
 
-// CTAs per unit of every GEMM of the step (host-side, from the grid geometry)
+// CTAs per unit of every GEMM of the step (host-side, from the grid
+// geometry), and the width of the row-statistics slots: 16 columns, or the
+// smallest row slice a statistics-producing GEMM (proj, out_c, mlp2) reduces
 inline int plan_splits(Ctx& c, int grid, int cl) {
-  const ee_expert& ex = c.ex;
-  const int d = ex.d_model, M = c.M;
-  const int shapes[7][3] = {{d, d, c.Rt}, {3 * d, d, M}, {d, d, M}, {d, d, M},
-                            {d, d, M}, {ex.hidden, d, M}, {d, ex.hidden, M}};
+  int shapes[7][3];
+  step_shapes(c, shapes);
+  int min_rows = kRU;
   for (int i = 0; i < 7; ++i) {
     const int sp = pick_split(shapes[i][0], shapes[i][1], shapes[i][2], grid / cl, cl, c.ks_cap);
     if (sp <= 0) return EE_ERR_UNSUPPORTED;
     int l = 0;
     while ((1 << l) < sp) ++l;
     c.lsplit[i] = l;
+    if ((i == 2 || i == 4 || i == 6) && (kRU >> l) < min_rows) min_rows = kRU >> l;
   }
+  c.stat_shift = min_rows >= 16 ? 4 : 3;
+  if (min_rows < 8) return EE_ERR_UNSUPPORTED;
+  c.n_slots = (c.ex.d_model + (1 << c.stat_shift) - 1) >> c.stat_shift;
   return EE_OK;
 }
 
