@@ -376,16 +376,19 @@ struct Gemm {
 
   // tcgen05 form of the MMAs: this CTA's KB k-blocks of the 128-row tile
   // `nt` against the staged activations (NP token rows, a multiple of 16).
-  // Per k-block the 256 threads dequantise the weights into A stage
-  // kb % kTcStages in TMEM (thread: row 32*(warp%4) + lane, k half warp/4),
-  // thread 0 issues eight 128 x NP x 16 MMAs into accumulator slot
-  // kb % kTcStages and commits them to the stage's mbarrier; a stage and slot
-  // are reused (k-block kb + kTcStages) only after those MMAs completed and
-  // the slot was drained. Slots are drained into registers with the block's
-  // fp32 scale (acc += scale * partial, in k-block order), so the arithmetic
-  // matches the mma.sync form: exact integer weights, fp32 sums, fp32 scale
-  // per k-block. Returns acc[i] = row 32*(warp%4) + lane, token
-  // 32*(warp/4) + i.
+  // k-blocks go in groups of up to kTcStages: the 256 threads dequantise the
+  // group's weights into A stages 0.. in TMEM (thread: row 32*(warp%4) +
+  // lane, k half warp/4), one CTA barrier, then thread 0 issues the group's
+  // 128 x NP x 16 MMAs back to back (eight per k-block, into accumulator slot
+  // kb % kTcStages) and commits each k-block to its stage's mbarrier. Issuing
+  // whole groups keeps the tensor pipe busy: an MMA of N <= 64 costs about
+  // the same as one of N = 64, and the pipe's start-up is paid once per
+  // group instead of once per k-block. A later group reuses a stage and slot
+  // after their MMAs completed and the slot was drained. Slots are drained
+  // into registers with the block's fp32 scale (acc += scale * partial, in
+  // k-block order), so the arithmetic matches the mma.sync form: exact
+  // integer weights, fp32 sums, fp32 scale per k-block. Returns acc[i] = row
+  // 32*(warp%4) + lane, token 32*(warp/4) + i.
   static EE_DEV void mma_tc(const GemmArgs& a, int nt, int kb0, int KB, int npre, int NP, uint32_t sx,
                             char* smem, const GemmSmem& sm, float (&acc)[32]) {
     const ee_linear& L = a.w;
@@ -426,42 +429,44 @@ struct Gemm {
       }
     };
 
-    auto issue = [&](int kb) {  // thread 0: the eight MMAs of k-block kb, committed to its stage
-      const int s = kb % kTcStages;
-      const uint32_t d = tmem + (uint32_t)(64 * s);
-      const uint32_t at = tmem + kTcACol + (uint32_t)(64 * s);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks)
-        umma_f16_ts(d, at + 8 * ks, umma_desc_sw128(sx + (uint32_t)((2 * kb + (ks >> 2)) * (kMTile * 128) + (ks & 3) * 32)),
-                    idesc, ks > 0 ? 1u : 0u);
-      umma_commit(bar + 8 * s);
-    };
-
     uint4 raw[CPT];
     fetch(0, raw);
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % kTcStages;
-      uint4 cur[CPT];
+    for (int g0 = 0; g0 < KB; g0 += kTcStages) {
+      const int gn = KB - g0 < kTcStages ? KB - g0 : kTcStages;
+      for (int i = 0; i < gn; ++i) {
+        const int kb = g0 + i;
+        uint4 cur[CPT];
 #pragma unroll
-      for (int j = 0; j < CPT; ++j) cur[j] = raw[j];
-      if (kb + 1 < KB) fetch(kb + 1, raw);
-      const float z = KIND == EE_W_UINT4Z ? zero_of(L, n, kb0 + kb) : 0.f;
-      if (kb >= kTcStages) {
-        wait_stage(s);  // k-block kb - kTcStages (stage s, slot s) is done
-        tc_fence_after();
-        drain(kb - kTcStages);
+        for (int j = 0; j < CPT; ++j) cur[j] = raw[j];
+        if (kb + 1 < KB) fetch(kb + 1, raw);
+        const float z = KIND == EE_W_UINT4Z ? zero_of(L, n, kb0 + kb) : 0.f;
+        if (g0 > 0) {
+          wait_stage(i);  // k-block kb - kTcStages (stage i, slot i) is done
+          tc_fence_after();
+          drain(kb - kTcStages);
+        }
+        uint32_t o[32];
+        dequant_tc(cur, z, o);
+        tmem_st32(tmem + lane_off + kTcACol + (uint32_t)(64 * i + 32 * kh), o);
       }
-      uint32_t o[32];
-      dequant_tc(cur, z, o);
-      tmem_st32(tmem + lane_off + kTcACol + (uint32_t)(64 * s + 32 * kh), o);
       tmem_wait_st();
       tc_fence_before();
       __syncthreads();
       if (threadIdx.x == 0) {
         tc_fence_after();
-        issue(kb);
+        for (int i = 0; i < gn; ++i) {
+          const int kb = g0 + i;
+          const uint32_t d = tmem + (uint32_t)(64 * i);
+          const uint32_t at = tmem + kTcACol + (uint32_t)(64 * i);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            umma_f16_ts(d, at + 8 * ks,
+                        umma_desc_sw128(sx + (uint32_t)((2 * kb + (ks >> 2)) * (kMTile * 128) + (ks & 3) * 32)),
+                        idesc, ks > 0 ? 1u : 0u);
+          umma_commit(bar + 8 * i);
+        }
       }
-      mask ^= 1u << s;
+      for (int i = 0; i < gn; ++i) mask ^= 1u << i;
     }
     // every MMA of the unit has completed once each used stage's last commit has
     for (int s = 0; s < kTcStages && s < KB; ++s) wait_stage(s);
