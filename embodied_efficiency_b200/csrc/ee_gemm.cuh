@@ -99,7 +99,7 @@ constexpr uint32_t kTcCols = 512;  // allocation: kTcStages * 128 columns
 constexpr uint32_t kTcBar = 0, kTcTmem = 8 * kTcStages, kTcMask = kTcTmem + 4, kTcStateBytes = 64;
 constexpr uint32_t kAuxGB = 0;                 // [2][2048] act: norm weight, bias slice
 constexpr uint32_t kAuxRow = 8192;             // [64][2] float: mean, rstd
-constexpr uint32_t kAuxBias = kAuxRow + 512;   // [128] float
+constexpr uint32_t kAuxBias = kAuxRow + 512;   // [128] act: bias slice
 constexpr uint32_t kAuxRes = kAuxBias + 512;   // [64][128] act: residual tile
 constexpr uint32_t kAuxScale = kAuxRes + 64 * 128 * 2;  // [kMaxKB][2][8 warps][8 g] float
 constexpr int kMaxKB = 16;                     // k-blocks per CTA with staged scales
@@ -321,8 +321,9 @@ struct Gemm {
   }
 
   // The unit's operands that no other CTA produces -- the norm weight / bias
-  // slice, the fp32 scales of every k-block, the bias -- into the aux area
-  // (cp.async, committed by the caller; the bias with plain loads).
+  // slice, the fp32 scales of every k-block, the bias slice -- into the aux
+  // area, all with cp.async (committed by the caller): when this runs between
+  // a CTA's grid-barrier arrive and wait nothing in it blocks.
   static EE_DEV void stage_const(const GemmArgs& a, int nt, const GemmSmem& sm, char* smem) {
     const uint32_t sbase = smem_u32(smem);
     const ee_linear& L = a.w;
@@ -364,13 +365,21 @@ struct Gemm {
                     sp + (size_t)n * ng + ((kb0 + kb) * kKBlock) / L.group);
         }
     }
-    // the last RPR threads load the bias (blocking loads): thread 0 stays free
-    // to poll the grid barrier when this runs between its arrive and wait
-    const int bt = threadIdx.x - (kThreads - RPR);
+    // bias slice: RPR/8 chunks of 8 values; copied with cp.async where N is a
+    // multiple of 8 and the bias 16-byte aligned (the sampler's layers), else
+    // loaded and stored (zeros without a bias or past N)
+    const int bt = threadIdx.x - (kThreads - RPR / 8);
     if (bt >= 0) {
-      float* sbias = reinterpret_cast<float*>(smem + sm.aux + kAuxBias);
-      const int n = nbase + bt;
-      sbias[bt] = (a.has_bias && n < L.n) ? ld_param(reinterpret_cast<const T*>(L.bias) + n) : 0.f;
+      const int n = nbase + 8 * bt;
+      const T* bp = reinterpret_cast<const T*>(L.bias);
+      T* sb = reinterpret_cast<T*>(smem + sm.aux + kAuxBias) + 8 * bt;
+      if (a.has_bias && (L.n % 8) == 0 && (reinterpret_cast<uintptr_t>(bp) & 15) == 0) {
+        const bool ok = n + 8 <= L.n;
+        cp_async16(sbase + sm.aux + kAuxBias + (uint32_t)(bt * 16), ok ? bp + n : bp, ok);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sb[e] = Act<T>::from_f((a.has_bias && n + e < L.n) ? ld_param(bp + n + e) : 0.f);
+      }
     }
   }
 
@@ -497,7 +506,7 @@ struct Gemm {
     const uint32_t sx = sbase + sm.x;
     char* aux = smem + sm.aux;
     float* rowst = reinterpret_cast<float*>(aux + kAuxRow);
-    float* sbias = reinterpret_cast<float*>(aux + kAuxBias);
+    const T* sbias = reinterpret_cast<const T*>(aux + kAuxBias);
     T* sres = reinterpret_cast<T*>(aux + kAuxRes);
 
     // weights: prefetched before the grid barrier, or requested now
@@ -780,9 +789,11 @@ struct Gemm {
         float v[8];
         uint4 rq = make_uint4(0, 0, 0, 0);
         if (a.epi == EPI_RESID) rq = *reinterpret_cast<const uint4*>(sres + tok * RPR + 8 * ch);
+        const uint4 bq = *reinterpret_cast<const uint4*>(sbias + 8 * ch);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          float y = Act<T>::round(E[tok * ES + 8 * ch + e] + sbias[8 * ch + e]);
+          const float2 bf = Act<T>::unpack2(comp(bq, e >> 1));
+          float y = Act<T>::round(E[tok * ES + 8 * ch + e] + ((e & 1) ? bf.y : bf.x));
           if (a.epi == EPI_GELU) {
             y = Act<T>::round(gelu_erf(y));
           } else if (a.epi == EPI_RESID) {
@@ -790,7 +801,7 @@ struct Gemm {
             y = Act<T>::round(((e & 1) ? rf.y : rf.x) + y);
           }
           v[e] = n0 + e < L.n ? y : 0.f;
-          E[tok * ES + 8 * ch + e] = v[e];  // final values for the row statistics
+          if (a.out_stats) E[tok * ES + 8 * ch + e] = v[e];  // final values for the row statistics
         }
         T* dst = out + (size_t)(m0 + tok) * a.ldo + n0;
         if (vec && n0 + 8 <= L.n) {
