@@ -218,9 +218,12 @@ EE_DEV float2 block_sum2(float a, float b, float* scratch /* [2 * kWarps] */) {
 // velocity store, then (head) x = in_proj(x_act) + b + temb(next step) with
 // its row statistics for the next first norm. Every load that does not
 // depend on this phase's arithmetic (the x row, the out_norm parameters, the
-// out_proj weights -- copied into the idle partial-tile buffers -- and the
-// Euler source values) is issued at entry.
-// Shared memory: d + 64 floats in the x region, out_proj in the p region.
+// out_proj weights -- copied into the idle partial-tile buffers --, the
+// in_proj weights -- copied into the rest of the x region and the idle
+// prefetch area -- and the Euler source values) is issued at entry.
+// Shared memory: d + 128 floats in the x region, out_proj in the p region,
+// in_proj rows [0, wi_split) after them in the x region, the others in the
+// pre area.
 template <typename T>
 EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head, char* smem) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -236,6 +239,15 @@ EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head,
   const T* Wo = reinterpret_cast<const T*>(c.ex.out_proj.weight);
   const bool wo_smem = do_tail && (size_t)A * d * 2 <= 2 * kPBytes;
   const uint32_t wo_s = smem_u32(smem) + c.sm.p;
+  // in_proj weights [d][A] (A * 2 bytes per row) into shared memory when they fit
+  const T* Wi = reinterpret_cast<const T*>(c.ex.in_proj.weight);
+  const uint32_t rowb = (uint32_t)A * 2u;
+  const uint32_t wi_a = smem_u32(smem) + c.sm.x + (uint32_t)(d + 128) * 4u;  // after hrow / xa / xs / red
+  const uint32_t wi_a_cap = (c.sm.p - c.sm.x) - (uint32_t)(d + 128) * 4u;
+  const int wi_split = (int)(wi_a_cap / rowb) < d ? (int)(wi_a_cap / rowb) : d;
+  const uint32_t wi_b = smem_u32(smem) + c.sm.pre;
+  const bool wi_smem = do_head && (size_t)(d - wi_split) * rowb <= c.sm.pre_bytes && (A % 8) == 0;
+  auto wi_addr = [&](int n) { return n < wi_split ? wi_a + (uint32_t)n * rowb : wi_b + (uint32_t)(n - wi_split) * rowb; };
   if (do_tail) {
     if (tid < nch) {
       xq = ld_act16(reinterpret_cast<const T*>(c.x) + (size_t)m * d + tid * 8);
@@ -253,9 +265,16 @@ EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head,
                                                            ((size_t)m * A + tid) * sizeof(T)));
     }
   }
+  if (wi_smem) {  // after the out_proj copies: the tail waits for those alone
+    const int cpr = A / 8;  // 16-byte chunks per row
+    for (int i = tid; i < d * cpr; i += kThreads) {
+      const int n = i / cpr, q = i - n * cpr;
+      cp_async16(wi_addr(n) + (uint32_t)q * 16u, Wi + (size_t)n * A + 8 * q, true);
+    }
+    cp_async_commit();
+  }
   const int bb = m / c.ex.horizon;
   const int trow = head_step * c.nbt + (c.nbt > 1 ? bb : 0);
-  const T* Wi = reinterpret_cast<const T*>(c.ex.in_proj.weight);
   const T* bi = reinterpret_cast<const T*>(c.ex.in_proj.bias);
   const T* temb = reinterpret_cast<const T*>(c.temb) + (size_t)trow * d;
 
@@ -302,25 +321,42 @@ EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head,
         hrow[tid * 8 + 2 * e + 1] = Act<T>::round(y1);
       }
     }
-    if (wo_smem) cp_async_wait<0>();
+    if (wo_smem) {
+      if (wi_smem) cp_async_wait<1>();
+      else cp_async_wait<0>();
+    }
     __syncthreads();
-    // ---- 3. out_proj: warp w computes outputs a = w, w+8, w+16, w+24 ----
+    // ---- 3. out_proj: warp w computes outputs a = w, w+8, w+16, w+24,
+    //         the four dot products interleaved (one hrow read for all) ----
     const T* ob = reinterpret_cast<const T*>(c.ex.out_proj.bias);
+    float accs[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int ch = lane; ch < nch; ch += 32) {
+      float hv[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int a = warp + kWarps * j;
-      if (a < A) {
-        float acc = 0.f;
-        for (int ch = lane; ch < nch; ch += 32) {
+      for (int e = 0; e < 8; ++e) hv[e] = hrow[ch * 8 + e];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int a = warp + kWarps * j;
+        if (a < A) {
           const uint4 wv = wo_smem ? lds16(wo_s + (uint32_t)(a * nch + ch) * 16u) : ld_weight16(Wo + (size_t)a * d + ch * 8);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f = Act<T>::unpack2(comp(wv, e));
-            acc = fmaf(hrow[ch * 8 + 2 * e], f.x, acc);
-            acc = fmaf(hrow[ch * 8 + 2 * e + 1], f.y, acc);
+            accs[j] = fmaf(hv[2 * e], f.x, accs[j]);
+            accs[j] = fmaf(hv[2 * e + 1], f.y, accs[j]);
           }
         }
-        acc = warp_sum(acc);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) accs[j] += __shfl_xor_sync(0xffffffffu, accs[j], o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int a = warp + kWarps * j;
+      if (a < A) {
+        const float acc = accs[j];
         if (lane == 0) {
           const float vel = Act<T>::round(acc + (ob ? ld_param(ob + a) : 0.f));
           T* xo = reinterpret_cast<T*>(c.x_out) + (size_t)m * A + a;
@@ -338,6 +374,7 @@ EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head,
     xa[tid] = Act<T>::to_f(reinterpret_cast<const T*>(c.x_in)[(size_t)m * A + tid]);
   }
   if (!do_head) return;
+  if (wi_smem) cp_async_wait<0>();
   __syncthreads();
   // ---- 4. in_proj + bias + t_proj(temb) for the head step; row statistics ----
   T* xr = reinterpret_cast<T*>(c.x) + (size_t)m * d;
@@ -364,7 +401,9 @@ EE_DEV void row_phase(const Ctx& c, int m, int step, bool do_tail, bool do_head,
   for (int n = tid; n < d; n += kThreads) {
     uint4 w4[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) w4[q] = q * 8 < A ? ld_weight16(Wi + (size_t)n * A + 8 * q) : make_uint4(0, 0, 0, 0);
+    for (int q = 0; q < 4; ++q)
+      w4[q] = q * 8 < A ? (wi_smem ? lds16(wi_addr(n) + (uint32_t)q * 16u) : ld_weight16(Wi + (size_t)n * A + 8 * q))
+                        : make_uint4(0, 0, 0, 0);
     one(n, w4, bi ? ld_param(bi + n) : 0.f, ld_act_scalar(temb + n));
   }
   const float2 tot = block_sum2(s, ss, red);
