@@ -82,7 +82,9 @@ struct GemmArgs {
 //   pre  weight words of the first unit, copied in before a grid barrier
 //   tc   (tcgen05 form) kTcStages mbarriers (MMA completion of each A
 //        stage) at +kTcBar, the TMEM base address at +kTcTmem and the parity
-//        of every barrier's commit count (bit s) at +kTcMask; the kernel
+//        of every barrier's commit count (bit s) at +kTcMask, the two
+//        mbarriers of the partial-tile receive buffers at +kTcPBar and the
+//        parity of their next phases (bit p) at +kTcPPar; the kernel
 //        initialises it and allocates TMEM
 struct GemmSmem {
   uint32_t x, p, aux, pre;
@@ -96,7 +98,8 @@ struct GemmSmem {
 constexpr int kTcStages = 4;
 constexpr uint32_t kTcACol = kTcStages * 64;
 constexpr uint32_t kTcCols = 512;  // allocation: kTcStages * 128 columns
-constexpr uint32_t kTcBar = 0, kTcTmem = 8 * kTcStages, kTcMask = kTcTmem + 4, kTcStateBytes = 64;
+constexpr uint32_t kTcBar = 0, kTcTmem = 8 * kTcStages, kTcMask = kTcTmem + 4, kTcPBar = kTcMask + 4,
+                   kTcPPar = kTcPBar + 16, kTcStateBytes = 64;
 constexpr uint32_t kAuxGB = 0;                 // [2][2048] act: norm weight, bias slice
 constexpr uint32_t kAuxRow = 8192;             // [64][2] float: mean, rstd
 constexpr uint32_t kAuxBias = kAuxRow + 512;   // [128] act: bias slice
@@ -509,6 +512,15 @@ struct Gemm {
     const T* sbias = reinterpret_cast<const T*>(aux + kAuxBias);
     T* sres = reinterpret_cast<T*>(aux + kAuxRes);
 
+    // tcgen05 form: partials arrive by st.async on this CTA's receive barrier
+    // for buffer `parity`; it expects S senders x RPR rows x the 4-token
+    // groups that hold real tokens (what the senders push)
+    const uint32_t pbar = sbase + sm.tc + kTcPBar + 8u * (uint32_t)parity;
+    const uint32_t ppar = TC ? ((*reinterpret_cast<volatile uint32_t*>(smem + sm.tc + kTcPPar) >> parity) & 1u) : 0u;
+    if (TC && active && threadIdx.x == 0) {
+      const int q0 = (min(32, mrows) + 3) >> 2, q1 = mrows > 32 ? (mrows - 32 + 3) >> 2 : 0;
+      mbar_arrive_expect_tx(pbar, (uint32_t)(S * RPR * (q0 + q1) * 16));
+    }
     // weights: prefetched before the grid barrier, or requested now
     PreRegs pr_local;
     const PreRegs* prw = pre;
@@ -735,10 +747,11 @@ struct Gemm {
         const int row = 32 * (warp & 3) + lane, t0 = 32 * (warp >> 2);
         const int owner = row >> rshift, lrow = row & (RPR - 1);
         const uint32_t dst = mapa(rbuf + (uint32_t)(((r * RPR + lrow) * kPS + t0) * 4), (uint32_t)(sub0 + owner));
+        const uint32_t dbar = mapa(pbar, (uint32_t)(sub0 + owner));
         const int nq = t0 < mrows ? (min(32, mrows - t0) + 3) >> 2 : 0;  // 4-token groups to send
 #pragma unroll
         for (int q = 0; q < 8; ++q)
-          if (q < nq) st_dsmem_f4(dst + 16 * q, acct[4 * q], acct[4 * q + 1], acct[4 * q + 2], acct[4 * q + 3]);
+          if (q < nq) st_async_f4(dst + 16 * q, acct[4 * q], acct[4 * q + 1], acct[4 * q + 2], acct[4 * q + 3], dbar);
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -754,7 +767,19 @@ struct Gemm {
           }
       }
     }
-    cluster_sync();  // every partial of this round has arrived
+    if (TC) {
+      // every partial of this round has arrived once the receive barrier's
+      // byte count has; the barrier chain also orders buffer reuse two
+      // rounds later (a sender pushes round rd+2 only after this CTA pushed
+      // round rd+1, i.e. after it summed round rd)
+      if (active) {
+        if (!mbar_wait(pbar, ppar, a.timeout_ns) && a.status) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
+        if (threadIdx.x == 0)
+          *reinterpret_cast<volatile uint32_t*>(smem + sm.tc + kTcPPar) ^= 1u << parity;
+      }
+    } else {
+      cluster_sync();  // every partial of this round has arrived
+    }
 
     // 6. sum the S partials of this CTA's RPR rows (local, source order)
     const int ES = RPR + 1;  // row stride of E (odd: the transposing writes below are conflict-free)

@@ -513,6 +513,9 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) mbar_init(tc_state + kTcBar + 8 * s, 1);
     *reinterpret_cast<uint32_t*>(smem + c.sm.tc + kTcMask) = 0;
+    mbar_init(tc_state + kTcPBar, 1);
+    mbar_init(tc_state + kTcPBar + 8, 1);
+    *reinterpret_cast<uint32_t*>(smem + c.sm.tc + kTcPPar) = 0;
     mbar_fence_init();
   }
   if (threadIdx.x < 32) {
