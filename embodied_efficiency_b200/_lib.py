@@ -49,7 +49,7 @@ class Expert(ctypes.Structure):
                 ("act_dtype", c_int32), ("norm_kind", c_int32), ("self_attn", c_int32),
                 ("reserved", c_int32), ("eps", c_float), ("reserved_f", c_float),
                 ("freqs", c_void_p), ("in_proj", Linear), ("t_proj", Linear), ("out_proj", Linear),
-                ("out_norm", Norm), ("blocks", c_void_p)]
+                ("out_norm", Norm), ("blocks", c_void_p), ("kv_maps", c_void_p)]
 
 
 # name -> (restype, argtypes); every symbol include/ee_b200.h declares
@@ -63,6 +63,8 @@ SIGNATURES = {
                              c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32,
                              c_void_p]),
     "ee_check_expert": (c_int32, [ctypes.POINTER(Expert), ctypes.POINTER(Block), c_int32, c_int32]),
+    "ee_encode_kv_maps": (c_int32, [ctypes.POINTER(Expert), ctypes.POINTER(Block), c_void_p, c_size_t,
+                                    c_void_p]),
     "ee_flow_sample_workspace_bytes": (c_size_t, [ctypes.POINTER(Expert), c_int32]),
     "ee_flow_sample": (c_int32, [ctypes.POINTER(Expert), c_void_p, c_void_p, c_void_p, c_int32,
                                  c_int32, c_void_p, c_size_t, c_void_p]),

@@ -5,13 +5,17 @@
 // is called in kernel/flow_expert.py:86,91.
 //
 // 8 warps = 4 query tiles of 16 rows x 2 key groups. Key blocks of 64 are
-// staged through shared memory with cp.async (double buffered, 16-byte
-// chunks XOR-swizzled by row so ldmatrix is conflict free); key group kg
-// takes blocks kg, kg+2, ... with an online softmax in fp32, and the two
-// groups' partial (max, sum, O) are merged through shared memory.
+// staged through shared memory (double buffered, 16-byte chunks XOR-swizzled
+// by row -- the 128-byte swizzle -- so ldmatrix is conflict free): with
+// cp.async, or, for keys / values no thread of the kernel writes (the cached
+// prefix of cross-attention, head size 64) and a tensor map of them, with
+// two TMA box loads per key block issued by one thread. Key group kg takes
+// blocks kg, kg+2, ... with an online softmax in fp32, and the two groups'
+// partial (max, sum, O) are merged through shared memory.
 #pragma once
 
 #include "ee_common.cuh"
+#include "ee_tma.cuh"
 
 namespace ee {
 
@@ -25,6 +29,12 @@ struct AttnArgs {
   int q_rows_per_b, k_rows_per_b;  // row offsets between batch elements
   int n_heads;
   float scale_log2;                // log2(e) / sqrt(hd)
+  // optional: tensor map of k / v ([rows][2 * n_heads * hd], 64 x 64 boxes,
+  // 128-byte swizzle; v at column n_heads * hd), for data not written while
+  // the kernel runs; waits give up after timeout_ns with EE_ERR_TIMEOUT in status
+  const CUtensorMap* kv_map;
+  int* status;
+  unsigned long long timeout_ns;
 };
 
 template <int HD>
@@ -35,7 +45,8 @@ struct AttnSmem {
   static constexpr int kKV = kQ + kTile;                // [stage][blk][K|V]
   static constexpr int kMerge = kKV + 2 * 2 * 2 * kTile;
   static constexpr int kMergeBytes = 4 * 16 * (HD + 2) * 4;
-  static constexpr int kTotal = kMerge + kMergeBytes;
+  static constexpr int kBar = kMerge + kMergeBytes;     // two mbarriers (TMA loads of each stage)
+  static constexpr int kTotal = kBar + 16;
 };
 
 EE_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -80,7 +91,21 @@ struct Attn {
     const int nkb = (a.n_k + 63) >> 6;
     const int npairs = (nkb + 1) >> 1;
 
+    const bool tma = HD == 64 && a.kv_map != nullptr;
+    const uint32_t bar = sbase + S::kBar;
     auto load_pair = [&](int pi, int st) {
+      if (tma) {
+        if (threadIdx.x == 0) {
+          const int nb = min(2, nkb - 2 * pi);
+          mbar_arrive_expect_tx(bar + 8 * st, (uint32_t)(nb * 2 * S::kTile));
+          for (int blk = 0; blk < nb; ++blk) {
+            const int row = (int)kr0 + (2 * pi + blk) * 64;  // keys past n_k read as zeros
+            tma_load_2d(sK(st, blk), a.kv_map, (int)col, row, bar + 8 * st);
+            tma_load_2d(sV(st, blk), a.kv_map, a.n_heads * HD + (int)col, row, bar + 8 * st);
+          }
+        }
+        return;
+      }
 #pragma unroll
       for (int blk = 0; blk < 2; ++blk) {
         const int kb = 2 * pi + blk;
@@ -92,6 +117,15 @@ struct Attn {
       }
     };
 
+    if (tma) {
+      // the barriers live in memory other phases reuse: initialise per unit
+      if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        mbar_init(bar + 8, 1);
+        mbar_fence_init();
+      }
+      __syncthreads();
+    }
     load_tile(sQ, a.q, a.ldq, col, qr0, a.n_q);
     load_pair(0, 0);
     cp_async_commit();
@@ -109,6 +143,8 @@ struct Attn {
       if (pi + 1 < npairs) load_pair(pi + 1, st ^ 1);
       cp_async_commit();
       cp_async_wait<1>();
+      if (tma && !mbar_wait(bar + 8 * st, (uint32_t)((pi >> 1) & 1), a.timeout_ns) && a.status)
+        atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
       __syncthreads();
       if (pi == 0) {
 #pragma unroll

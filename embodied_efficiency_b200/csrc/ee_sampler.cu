@@ -1,5 +1,7 @@
 // ee_sampler.cu -- C ABI of the fused sampler (kernels in ee_sampler.cuh,
 // instantiated per activation dtype / head size in ee_sampler_<dtype>_<hd>.cu).
+#include <vector>
+
 #include "ee_sampler.cuh"
 
 namespace ee {
@@ -31,6 +33,30 @@ int ee_check_expert(const ee_expert* ex, const ee_block* host_blocks, int32_t n_
   int rc = validate_expert(*ex, n_steps, mode);
   if (rc) return rc;
   return validate_blocks(*ex, host_blocks);
+}
+
+int ee_encode_kv_maps(const ee_expert* ex, const ee_block* host_blocks, void* maps, size_t maps_bytes,
+                      ee_stream_t stream) {
+  if (!ex || !host_blocks || !maps) return EE_ERR_ARG;
+  if (ex->n_layers < 1 || ex->n_heads < 1 || ex->batch < 1 || ex->prefix_len < 1) return EE_ERR_SHAPE;
+  if (ex->d_model % ex->n_heads || ex->d_model / ex->n_heads != 64) return EE_ERR_UNSUPPORTED;
+  if (maps_bytes < (size_t)ex->n_layers * sizeof(CUtensorMap)) return EE_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(maps) & 63) return EE_ERR_ALIGN;
+  int rc = check_device();
+  if (rc) return rc;
+  std::vector<CUtensorMap> h((size_t)ex->n_layers);
+  const uint64_t cols = 2 * (uint64_t)ex->d_model, rows = (uint64_t)ex->batch * ex->prefix_len;
+  for (int l = 0; l < ex->n_layers; ++l) {
+    if (!host_blocks[l].kv) return EE_ERR_ARG;
+    if (!make_tmap_2d(&h[l], host_blocks[l].kv, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, cols, rows, cols * 2, 64, 64,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+      return EE_ERR_ALIGN;
+  }
+  if (cudaMemcpyAsync(maps, h.data(), h.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice,
+                      (cudaStream_t)stream) != cudaSuccess)
+    return EE_ERR_LAUNCH;
+  // pageable source: the copy has been staged when the call returns
+  return EE_OK;
 }
 
 size_t ee_flow_sample_workspace_bytes(const ee_expert* ex, int32_t n_steps) {

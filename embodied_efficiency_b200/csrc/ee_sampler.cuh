@@ -576,7 +576,10 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
           at.v = kv + d; at.ldv = 2 * d;
           at.n_k = c.ex.prefix_len;
           at.k_rows_per_b = c.ex.prefix_len;
+          if (c.ex.kv_maps) at.kv_map = reinterpret_cast<const CUtensorMap*>(c.ex.kv_maps) + ph.layer;
         }
+        at.status = c.status;
+        at.timeout_ns = c.timeout_ns;
         at.out = c.att; at.ldo = d;
         at.n_q = c.ex.horizon;
         at.q_rows_per_b = c.ex.horizon;

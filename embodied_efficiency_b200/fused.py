@@ -120,6 +120,16 @@ class FusedPlan:
         lib = _lib.load()
         _lib.check(lib.ee_check_expert(ctypes.byref(ex), blocks, 1, _lib.EE_MODE_EULER),
                    "ee_check_expert")
+        # TMA descriptors of the cached prefix K/V (head size 64): the
+        # cross-attention then loads K/V tiles with TMA instead of cp.async
+        self.kv_maps = None
+        if d // cfg.n_heads == 64:
+            maps = torch.empty(cfg.n_layers * 128, dtype=torch.uint8, device=self.device)
+            rc = lib.ee_encode_kv_maps(ctypes.byref(ex), blocks, maps.data_ptr(), maps.numel(),
+                                       _lib.stream_ptr(self.device))
+            if rc == 0:
+                self.kv_maps = maps
+                ex.kv_maps = maps.data_ptr()
         self._ws = {}
 
     # -- record builders ---------------------------------------------------

@@ -23,6 +23,7 @@
  *   ee_flow_sample_geometry   launch geometry of the fused sampler (new)
  *   ee_flow_sample_traced / ee_flow_sample_phases   per-phase device timeline (new)
  *   ee_read_status        device status word of a sampler workspace (new)
+ *   ee_encode_kv_maps     TMA descriptors of the cached prefix K/V (new)
  *   ee_barrier_selftest   bounded-wait self-test of the grid barrier (new)
  *   ee_strerror / ee_version / ee_struct_size   (new)
  */
@@ -139,7 +140,21 @@ typedef struct ee_expert {
   ee_linear in_proj, t_proj, out_proj;
   ee_norm out_norm;
   const ee_block* blocks; /* DEVICE pointer to n_layers ee_block records */
+  /* Optional DEVICE pointer to n_layers 128-byte tensor maps (64-byte
+   * aligned) of the blocks' cached prefix K/V, written by ee_encode_kv_maps;
+   * with them the cross-attention loads K/V with TMA, without (NULL) it
+   * copies them with cp.async. */
+  const void* kv_maps;
 } ee_expert;
+
+/* Encode the tensor maps of every block's cached prefix K/V ([batch *
+ * prefix_len][2 d] of the act dtype, as ee_block.kv points to) into the
+ * device buffer `maps` (n_layers * 128 bytes, 64-byte aligned), copied on
+ * `stream`. Head size 64 only (EE_ERR_UNSUPPORTED otherwise). `host_blocks`
+ * is a HOST copy of the block table, as for ee_check_expert. New: no
+ * counterpart in the reference. */
+int ee_encode_kv_maps(const ee_expert* ex, const ee_block* host_blocks, void* maps, size_t maps_bytes,
+                      ee_stream_t stream);
 
 /* Tracing variant of ee_flow_sample: when `trace` is not NULL, thread 0 of
  * every CTA writes two %globaltimer stamps (ns) per phase p:

@@ -202,3 +202,23 @@ def test_config5_scale_against_oracle(cuda):
     qp = OS.quantize_params(p, ocfg, 4)
     ref = OS.flow_sample(p, ocfg, x0.bfloat16(), 2, OS.encode_prefix(p, ocfg, prefix.bfloat16(), qp), qp).float()
     assert OS.action_error(y, ref) < 0.05
+
+
+@pytest.mark.parametrize("tag,batch", [("small", 1), ("small", 3), ("ref", 1), ("ref", 2)])
+def test_prefix_kv_tma_matches_cp_async(cuda, tag, batch):
+    """Cross-attention reads the cached prefix K/V with TMA when the plan has
+    tensor maps of it (ee_encode_kv_maps) and with cp.async without: the same
+    bytes reach shared memory, so the actions are identical (partial key
+    blocks, several requests and several key-block pairs included)."""
+    from embodied_efficiency_b200 import fused
+    m, cfg, params, x0, prefix = build_model(CFGS[tag], 4, batch=batch)
+    plan = fused.FusedPlan(m, batch, m.encode(prefix.cuda().bfloat16()))
+    assert plan.kv_maps is not None and plan.ex.kv_maps
+    x = x0.cuda().bfloat16()
+    with_maps = plan.run(x, 10)
+    assert plan.status(10) == 0
+    plan.ex.kv_maps = None
+    without = plan.run(x, 10)
+    torch.cuda.synchronize()
+    assert plan.status(10) == 0
+    assert torch.equal(with_maps, without)
