@@ -1,6 +1,6 @@
 """GPU parity of the int4 packing and the dequant-GEMM (ee_pack_int4 /
 ee_unpack_int4 / ee_wq_gemm) against the CPU oracle and the reference's
-golden outputs. Tolerance (north_star): max|Y - Y_ref| / max|Y_ref| <= 2e-2."""
+golden outputs. Tolerance (the path's bf16 gate): max|Y - Y_ref| / max|Y_ref| <= 2e-2."""
 import numpy as np
 import pytest
 import torch

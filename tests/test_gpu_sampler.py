@@ -1,5 +1,5 @@
 """GPU parity of the fused sampler (ee_flow_sample) against the reference's
-golden outputs and the CPU oracle. Tolerance (north_star): action error
+golden outputs and the CPU oracle. Tolerance (the path's bf16 gate): action error
 (rMSE / mean|ref|, kernel/quant.py:104-105) <= 5% after 10 Euler steps."""
 import ctypes
 
