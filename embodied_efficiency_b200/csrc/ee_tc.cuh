@@ -349,8 +349,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 
     // ---------------- epilogue part 1: TMEM -> registers ----------------
-    if (!mbar_wait(bar_acc, 0, a.timeout_ns) && lane == 0) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
-    tc_fence_after();
     const int q4 = warp & 3, quarter = warp >> 2;
     const int r = 32 * q4 + lane;  // weight row of the tile
     const int n = n0 + r;
@@ -360,11 +358,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int c_beg = quarter * CPQ * 16;
     const int c_end = quarter < NCH ? c_beg + CPQ * 16 : c_beg;
     const int RS = 128 >> a.lsplit;
+    // residual values of this thread's outputs, requested before the wait for
+    // the accumulators so that they arrive while the last MMAs complete
+    T resv[CPQ * 16];
+    if (S == 1 && a.epi == EPI_RESID && n < L.n) {
+      const T* res = reinterpret_cast<const T*>(a.resid);
+#pragma unroll
+      for (int i = 0; i < CPQ * 16; ++i) {
+        const int tok = m0 + c_beg + i;
+        if (c_beg + i < c_end && tok < a.M) resv[i] = res[(size_t)tok * a.ldr + n];
+      }
+    }
+    if (!mbar_wait(bar_acc, 0, a.timeout_ns) && lane == 0) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
+    tc_fence_after();
     if (S == 1) {
       const float bias = (a.has_bias && n < L.n) ? ld_param(reinterpret_cast<const T*>(L.bias) + n) : 0.f;
       T* out = reinterpret_cast<T*>(a.out);
-      const T* res = reinterpret_cast<const T*>(a.resid);
-      for (int c0 = c_beg; c0 < c_end; c0 += 16) {
+#pragma unroll
+      for (int cc = 0; cc < CPQ; ++cc) {
+        const int c0 = c_beg + 16 * cc;
+        if (c0 >= c_end) break;
         uint32_t v[16];
         tmem_ld16(tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)c0, v);
         tmem_wait_ld();
@@ -377,7 +390,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               if (a.epi == EPI_GELU) {
                 y = Act<T>::round(gelu_erf(y));
               } else if (a.epi == EPI_RESID) {
-                y = Act<T>::round(ld_param(res + (size_t)tok * a.ldr + n) + y);
+                y = Act<T>::round(Act<T>::to_f(resv[16 * cc + e]) + y);
               }
               out[(size_t)tok * a.ldo + n] = Act<T>::from_f(y);
             }
