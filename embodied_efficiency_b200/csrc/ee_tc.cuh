@@ -534,11 +534,22 @@ int tc_launch_k(const GemmArgs& g, const TcShape& sh, int* status, cudaStream_t 
   const int ps = NT + 4;
   const uint32_t recv = S > 1 ? (uint32_t)(S * RS * ps * 4) : 0u;
   const int na = dq ? 2 : 0;
-  const uint32_t fixed = (uint32_t)na * 32768u + 8u * 40u + 16u + recv + 16u + 1024u + 3u * 2u * kTcDqThreads * 4u * 2u + 16u;
-  if ((uint32_t)dp->smem_optin <= fixed + stage) return EE_OK;
-  int ns = (int)(((uint32_t)dp->smem_optin - fixed) / stage);
-  ns = ns < 8 ? ns : 8;
-  ns = ns < kbc ? ns : kbc;
+  constexpr uint32_t items = KIND == EE_W_INT8 ? 2u : 1u;
+  const uint32_t scbytes = dq ? 3u * items * kTcDqThreads * 4u * (KIND == EE_W_UINT4Z ? 2u : 1u) : 0u;
+  const uint32_t ebytes = (uint32_t)(((NT + 3) & ~3) * RS * 4);  // owner's summed tile (reuses the ring)
+  // shared memory of a launch with ns stages: the layout below, computed the same way
+  auto smem_for = [&](int ns_) -> size_t {
+    uint32_t ring_end = (uint32_t)ns_ * stage + (uint32_t)na * 32768u;
+    if (ring_end < ebytes) ring_end = ebytes;
+    const uint32_t off_bar = tc_align(ring_end, 16u);
+    const uint32_t off_tm = off_bar + 8u * (2u * (uint32_t)ns_ + 2u * (uint32_t)(dq ? na : 1) + 1u);
+    const uint32_t off_recv = tc_align(off_tm + 4u, 16u);
+    const uint32_t off_sc = tc_align(off_recv + recv, 16u);
+    return (size_t)off_sc + scbytes + 1024;
+  };
+  // as many stages as fit (at most 8, at most the k-blocks)
+  int ns = kbc < 8 ? kbc : 8;
+  while (ns > 0 && smem_for(ns) > (size_t)dp->smem_optin) --ns;
   if (ns < 1) return EE_OK;
 
   TcArgs a{};
@@ -560,13 +571,10 @@ int tc_launch_k(const GemmArgs& g, const TcShape& sh, int* status, cudaStream_t 
   a.off_a = (uint32_t)ns * stage;
   uint32_t ring_end = a.off_a + (uint32_t)na * 32768u;
   // the owner's summed tile reuses the ring
-  const uint32_t ebytes = (uint32_t)(((NT + 3) & ~3) * RS * 4);
   if (ring_end < ebytes) ring_end = ebytes;
   a.off_bar = tc_align(ring_end, 16u);
   a.off_tm = a.off_bar + 8u * (2u * ns + 2u * (uint32_t)a.na + 1u);
   a.off_recv = tc_align(a.off_tm + 4u, 16u);
-  constexpr uint32_t items = KIND == EE_W_INT8 ? 2u : 1u;
-  const uint32_t scbytes = dq ? 3u * items * kTcDqThreads * 4u * (KIND == EE_W_UINT4Z ? 2u : 1u) : 0u;
   a.off_sc = tc_align(a.off_recv + recv, 16u);
   const size_t smem = (size_t)a.off_sc + scbytes + 1024;
   if (smem > (size_t)dp->smem_optin) return EE_OK;
