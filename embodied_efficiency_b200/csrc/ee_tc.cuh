@@ -43,6 +43,7 @@ constexpr int kTcDqThreads = kTcDqWarps * 32;
 constexpr int kTcProdWarp = kTcDqWarps, kTcMmaWarp = kTcDqWarps + 1;
 constexpr int kTcWarps = kTcDqWarps + 2;
 constexpr int kTcThreads = kTcWarps * 32;
+constexpr uint32_t kTcpEpiBytes = 4u * 16u * 32u * 2u;  // 4 epilogue warps x [16 tokens][32 rows] of 16-bit
 
 struct TcArgs {
   ee_linear w;
@@ -62,6 +63,7 @@ struct TcArgs {
   uint32_t stage_bytes;
   uint32_t off_a, off_bar, off_recv, off_tm;
   uint32_t off_sc;   // scale / zero-point ring [3 slots][2][256 threads][ITEMS] 4-byte words
+  uint32_t off_ep;   // persistent form: per epilogue warp a [16 tokens][32 rows] staging tile
   int* status;
   unsigned long long timeout_ns;
 };
@@ -120,6 +122,35 @@ struct TcDequant {
     const uint32_t addr = abase + (uint32_t)(c >> 3) * 16384u + sw128(row, c & 7);
     asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v0), "r"(v1), "r"(v2), "r"(v3)
                  : "memory");
+  }
+  // One dequantising item: the raw 16-byte chunk `ch` of weight row `row`
+  // in the TMA stage `st` -> q * scale (scale rounded to the activation type)
+  // into the A tile `ab`.
+  static EE_DEV void item(uint32_t st, uint32_t ab, int row, int ch, float scv, float zcv) {
+    const uint32_t s2 = Act<T>::pack2(scv, scv);
+    if (KIND == EE_W_INT8) {
+      const uint4 raw = lds16(st + sw128(row, ch));
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint32_t w0 = comp(raw, 2 * u) ^ 0x80808080u, w1 = comp(raw, 2 * u + 1) ^ 0x80808080u;
+        st_a(ab, row, 2 * ch + u, hmul2<T>(int8_pair<T>(w0, 0, 1), s2), hmul2<T>(int8_pair<T>(w0, 2, 3), s2),
+             hmul2<T>(int8_pair<T>(w1, 0, 1), s2), hmul2<T>(int8_pair<T>(w1, 2, 3), s2));
+      }
+    } else {
+      // 64-byte swizzle: chunk index XOR bits [7,9) of the row offset
+      const uint4 raw = lds16(st + (uint32_t)(row * 64 + ((ch ^ ((row >> 1) & 3)) << 4)));
+      const float zoff = KIND == EE_W_INT4 ? 8.0f : zcv;
+      const uint32_t xor8 = KIND == EE_W_INT4 ? 0x00080008u : 0u;
+      const uint32_t nego = Act<T>::neg_offset2(Act<T>::kInt4Base + zoff);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t w = comp(raw, u), w4 = w >> 4;
+        uint32_t o[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) o[p] = hmul2<T>(fma2<T>(nib_pair<T>(w, w4, p, xor8), Act<T>::kOne2, nego), s2);
+        st_a(ab, row, 4 * ch + u, o[0], o[1], o[2], o[3]);
+      }
+    }
   }
 };
 
@@ -307,32 +338,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           float scv, zcv;
           TcDequant<T, KIND>::read_sz(L, rowsi[i] + gcur, scr + (uint32_t)r3 * kSlot + (uint32_t)i * (kTcDqThreads * 4u), kZoff,
                                       scv, zcv);
-          const uint32_t s2 = Act<T>::pack2(scv, scv);
-          if (KIND == EE_W_INT8) {
-            const uint4 raw = lds16(st + sw128(row, ch));
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const uint32_t w0 = comp(raw, 2 * u) ^ 0x80808080u, w1 = comp(raw, 2 * u + 1) ^ 0x80808080u;
-              TcDequant<T, KIND>::st_a(ab, row, 2 * ch + u, hmul2<T>(int8_pair<T>(w0, 0, 1), s2),
-                                       hmul2<T>(int8_pair<T>(w0, 2, 3), s2), hmul2<T>(int8_pair<T>(w1, 0, 1), s2),
-                                       hmul2<T>(int8_pair<T>(w1, 2, 3), s2));
-            }
-          } else {
-            // 64-byte swizzle: chunk index XOR bits [7,9) of the row offset
-            const uint4 raw = lds16(st + (uint32_t)(row * 64 + ((ch ^ ((row >> 1) & 3)) << 4)));
-            const float zoff = KIND == EE_W_INT4 ? 8.0f : zcv;
-            const uint32_t xor8 = KIND == EE_W_INT4 ? 0x00080008u : 0u;
-            const uint32_t nego = Act<T>::neg_offset2(Act<T>::kInt4Base + zoff);
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const uint32_t w = comp(raw, u), w4 = w >> 4;
-              uint32_t o[4];
-#pragma unroll
-              for (int p = 0; p < 4; ++p)
-                o[p] = hmul2<T>(fma2<T>(nib_pair<T>(w, w4, p, xor8), Act<T>::kOne2, nego), s2);
-              TcDequant<T, KIND>::st_a(ab, row, 4 * ch + u, o[0], o[1], o[2], o[3]);
-            }
-          }
+          TcDequant<T, KIND>::item(st, ab, row, ch, scv, zcv);
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -476,6 +482,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+}  // namespace ee
+
+#include "ee_tcp.cuh"
+
+namespace ee {
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -542,10 +554,10 @@ int tc_launch_k(const GemmArgs& g, const TcShape& sh, int* status, cudaStream_t 
     uint32_t ring_end = (uint32_t)ns_ * stage + (uint32_t)na * 32768u;
     if (ring_end < ebytes) ring_end = ebytes;
     const uint32_t off_bar = tc_align(ring_end, 16u);
-    const uint32_t off_tm = off_bar + 8u * (2u * (uint32_t)ns_ + 2u * (uint32_t)(dq ? na : 1) + 1u);
+    const uint32_t off_tm = off_bar + 8u * (2u * (uint32_t)ns_ + 2u * (uint32_t)(dq ? na : 1) + 4u);
     const uint32_t off_recv = tc_align(off_tm + 4u, 16u);
     const uint32_t off_sc = tc_align(off_recv + recv, 16u);
-    return (size_t)off_sc + scbytes + 1024;
+    return (size_t)tc_align(off_sc + scbytes, 16u) + kTcpEpiBytes + 1024;
   };
   // as many stages as fit (at most 8, at most the k-blocks)
   int ns = kbc < 8 ? kbc : 8;
@@ -573,10 +585,13 @@ int tc_launch_k(const GemmArgs& g, const TcShape& sh, int* status, cudaStream_t 
   // the owner's summed tile reuses the ring
   if (ring_end < ebytes) ring_end = ebytes;
   a.off_bar = tc_align(ring_end, 16u);
-  a.off_tm = a.off_bar + 8u * (2u * ns + 2u * (uint32_t)a.na + 1u);
+  // stage / A-tile barriers, then the accumulator barrier(s): one for
+  // wq_tc_kernel, two full + two drained for wq_tcp_kernel
+  a.off_tm = a.off_bar + 8u * (2u * ns + 2u * (uint32_t)a.na + 4u);
   a.off_recv = tc_align(a.off_tm + 4u, 16u);
   a.off_sc = tc_align(a.off_recv + recv, 16u);
-  const size_t smem = (size_t)a.off_sc + scbytes + 1024;
+  a.off_ep = tc_align(a.off_sc + scbytes, 16u);
+  const size_t smem = (size_t)a.off_ep + kTcpEpiBytes + 1024;
   if (smem > (size_t)dp->smem_optin) return EE_OK;
   a.status = status;
   a.timeout_ns = 1000000000ull;
@@ -591,6 +606,22 @@ int tc_launch_k(const GemmArgs& g, const TcShape& sh, int* status, cudaStream_t 
                     (uint64_t)g.ldx * 2u, 64u, (uint32_t)NT, CU_TENSOR_MAP_SWIZZLE_128B))
     return EE_OK;
 
+  if (S == 1 && sh.tiles > (long long)dp->sms && g.epi != EPI_GELU) {
+    // more tiles than SMs: the persistent form, one CTA per SM looping over
+    // tiles with the epilogue of one tile overlapping the next (not for the
+    // GELU epilogue, whose erf work on four warps outlasts the overlapped
+    // main loop: 323 vs 273 us at 12800 x 4096 x 1024)
+    auto fnp = wq_tcp_kernel<T, KIND, NT>;
+    static std::atomic<int> smem_set_p[64];
+    allow_max_smem(fnp, smem_set_p);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)dp->sms);
+    cfg.blockDim = dim3(kTcpThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    *used = true;
+    return cudaLaunchKernelEx(&cfg, fnp, tw, tx, a) == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
+  }
   auto fn = wq_tc_kernel<T, KIND, NT>;
   static std::atomic<int> smem_set[64];
   allow_max_smem(fn, smem_set);

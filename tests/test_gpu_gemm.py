@@ -159,6 +159,28 @@ def test_epilogues_and_fp16(cuda, kind):
     assert rel_err(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("kind", ["int8", "int4", "int4z", "bf16"])
+def test_more_tiles_than_sms(cuda, kind):
+    """M=2600, N=2048, K=256: 11 x 16 tiles of 256 tokens, more than the SMs,
+    so the persistent form of the tensor-core GEMM runs (tiles looped per CTA,
+    epilogue overlapped, a ragged last token tile) -- bias, GELU and residual
+    epilogues against the oracle."""
+    rng = np.random.default_rng(29)
+    m, n, k = 2600, 2048, 256
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    b = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    grp = 128 if kind != "bf16" else 0
+    y, ref = _run(cuda, x, w, kind, grp, bias=b)
+    assert rel_err(y, ref) <= TOL
+    r = rng.standard_normal((m, n)).astype(np.float32)
+    y, ref = _run(cuda, x, w, kind, grp, bias=b, residual=r)
+    assert rel_err(y, ref) <= TOL
+    if kind == "int4":
+        y, ref = _run(cuda, x, w, kind, grp, bias=b, gelu=True)
+        assert rel_err(y, ref) <= TOL
+
+
 def test_fp32_activations_and_errors(cuda):
     from embodied_efficiency_b200 import wq_linear
     rng = np.random.default_rng(5)
