@@ -43,7 +43,8 @@ constexpr int kTcDqThreads = kTcDqWarps * 32;
 constexpr int kTcProdWarp = kTcDqWarps, kTcMmaWarp = kTcDqWarps + 1;
 constexpr int kTcWarps = kTcDqWarps + 2;
 constexpr int kTcThreads = kTcWarps * 32;
-constexpr uint32_t kTcpEpiBytes = 4u * 16u * 32u * 2u;  // 4 epilogue warps x [16 tokens][32 rows] of 16-bit
+constexpr int kTcpEpiWarps = 8;  // epilogue warps of the persistent form (ee_tcp.cuh)
+constexpr uint32_t kTcpEpiBytes = (uint32_t)kTcpEpiWarps * 16u * 32u * 2u;  // per warp [16 tokens][32 rows] of 16-bit
 
 struct TcArgs {
   ee_linear w;
@@ -606,11 +607,9 @@ int tc_launch_k(const GemmArgs& g, const TcShape& sh, int* status, cudaStream_t 
                     (uint64_t)g.ldx * 2u, 64u, (uint32_t)NT, CU_TENSOR_MAP_SWIZZLE_128B))
     return EE_OK;
 
-  if (S == 1 && sh.tiles > (long long)dp->sms && g.epi != EPI_GELU) {
+  if (S == 1 && sh.tiles > (long long)dp->sms) {
     // more tiles than SMs: the persistent form, one CTA per SM looping over
-    // tiles with the epilogue of one tile overlapping the next (not for the
-    // GELU epilogue, whose erf work on four warps outlasts the overlapped
-    // main loop: 323 vs 273 us at 12800 x 4096 x 1024)
+    // tiles with the epilogue of one tile overlapping the next
     auto fnp = wq_tcp_kernel<T, KIND, NT>;
     static std::atomic<int> smem_set_p[64];
     allow_max_smem(fnp, smem_set_p);

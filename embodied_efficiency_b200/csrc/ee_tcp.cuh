@@ -1,10 +1,10 @@
 // ee_tcp.cuh -- persistent form of the tcgen05 dequant-GEMM (ee_tc.cuh) for
-// calls with more tiles than SMs, no split of K and a store or residual
-// epilogue: one CTA per SM loops over tiles (tile = blockIdx.x,
+// calls with more tiles than SMs and no split of K: one CTA per SM loops over
+// tiles (tile = blockIdx.x,
 // blockIdx.x + gridDim.x, ...), and the epilogue of a tile overlaps the next
 // tile's loads, dequantisation and MMAs.
 //
-// Roles (22 warps):
+// Roles (26 warps):
 //   warps 0-15   dequantisers, as in ee_tc.cuh; their k-block sequence runs
 //                on across tiles
 //   warp 16      TMA producer: raw weights and activations of every k-block
@@ -12,8 +12,8 @@
 //   warp 17      TMEM allocator and MMA issuer: tile i accumulates into TMEM
 //                buffer i % 2 (two buffers of TMC columns) once the epilogue
 //                has drained that buffer's previous tile
-//   warps 18-21  epilogue: one warp per 32-lane quarter of TMEM, all NT
-//                columns in 16-token chunks: bias (and GELU) per lane, the
+//   warps 18-25  epilogue: two warps per 32-lane quarter of TMEM, half of
+//                the NT columns each, in 16-token chunks: bias (and GELU) per lane, the
 //                chunk staged through shared memory as [16 tokens][32 rows],
 //                then per lane 16-byte residual loads (one chunk ahead) and
 //                16-byte stores; the buffer is then released to the MMA issuer
@@ -26,7 +26,7 @@
 namespace ee {
 
 constexpr int kTcpEpiWarp0 = kTcDqWarps + 2;  // first epilogue warp
-constexpr int kTcpWarps = kTcDqWarps + 6;
+constexpr int kTcpWarps = kTcDqWarps + 2 + kTcpEpiWarps;
 constexpr int kTcpThreads = kTcpWarps * 32;
 
 template <typename T, int KIND, int NT>
@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(kTcpThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_accf + 8u * b, 1);
-      mbar_init(bar_acce + 8u * b, 4);  // the four epilogue warps
+      mbar_init(bar_acce + 8u * b, kTcpEpiWarps);  // the epilogue warps
     }
     mbar_fence_init();
   }
@@ -169,8 +169,11 @@ __global__ void __launch_bounds__(kTcpThreads, 1)
     }
     __syncwarp();
   } else if (warp >= kTcpEpiWarp0) {
-    // ---------------- epilogue: one 32-lane quarter of TMEM per warp ----------------
-    const int q4 = warp & 3;  // warps 18-21 cover quarters 2, 3, 0, 1
+    // ---------------- epilogue: two warps per 32-lane quarter of TMEM ----------------
+    const int q4 = warp & 3;  // warps 18-25 cover quarters 2, 3, 0, 1, 2, 3, 0, 1
+    const int half = (warp - kTcpEpiWarp0) >> 2;  // which half of the columns
+    constexpr int HC = NT >= 32 ? NT / 2 : NT;     // columns per half (a multiple of 16)
+    const int cbeg = half * HC, cend = NT >= 32 ? cbeg + HC : (half == 0 ? NT : 0);
     const int r = 32 * q4 + lane;
     bool ok = true;
     for (int i = 0; i < my_tiles && ok; ++i) {
@@ -200,15 +203,15 @@ __global__ void __launch_bounds__(kTcpThreads, 1)
         }
       };
       uint4 rq_cur[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, rq_nxt[2] = {rq_cur[0], rq_cur[1]};
-      if (vres) load_res(0, rq_cur);
+      if (vres && cbeg < cend) load_res(cbeg, rq_cur);
       if (!mbar_wait(bar_accf + 8u * buf, (uint32_t)((i >> 1) & 1), a.timeout_ns)) {
         if (lane == 0) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
         ok = false;
         break;
       }
       tc_fence_after();
-      for (int c0 = 0; c0 < NT; c0 += 16) {
-        if (vres && c0 + 16 < NT) load_res(c0 + 16, rq_nxt);
+      for (int c0 = cbeg; c0 < cend; c0 += 16) {
+        if (vres && c0 + 16 < cend) load_res(c0 + 16, rq_nxt);
         uint32_t v[16];
         tmem_ld16(tmem + (uint32_t)buf * TMC + ((uint32_t)(32 * q4) << 16) + (uint32_t)c0, v);
         tmem_wait_ld();
