@@ -77,6 +77,27 @@ def _norm(cfg):
         else nn.LayerNorm(cfg.d_model)
 
 
+def _apply_norm(mod, x):
+    """The blocks' norm on the layer-by-layer path: nn.LayerNorm of bf16 / fp16
+    CUDA activations on the sm_100a row kernel (``ee_layer_norm``: fp32
+    statistics, nn.LayerNorm's formula and one rounding); other norms and
+    shapes run the module itself."""
+    d = x.shape[-1]
+    if (isinstance(mod, nn.LayerNorm) and x.is_cuda and x.dtype in (torch.bfloat16, torch.float16)
+            and d % 8 == 0 and d <= 2048 and mod.weight is not None and mod.weight.dtype == x.dtype
+            and (mod.bias is None or mod.bias.dtype == x.dtype)):
+        xf = x.reshape(-1, d)
+        if not xf.is_contiguous() or xf.data_ptr() % 16:
+            xf = xf.contiguous()
+        y = torch.empty_like(xf)
+        _lib.check(_lib.load().ee_layer_norm(xf.data_ptr(), mod.weight.data_ptr(), _lib.ptr(mod.bias),
+                                             y.data_ptr(), xf.shape[0], d, d, d, float(mod.eps),
+                                             _lib.act_code(x.dtype), _lib.stream_ptr(x.device)),
+                   "ee_layer_norm")
+        return y.reshape(x.shape)
+    return mod(x)
+
+
 def _apply_linear(mod, x, gelu: bool = False, residual=None):
     """A linear of the eager path on the sm_100a GEMM (cuBLAS only for K % 128 != 0),
     with GELU or ``residual +`` fused into the GEMM epilogue (the same roundings
@@ -135,13 +156,13 @@ class Block(nn.Module):
         """Eager GPU composition (used only where the fused launch does not apply)."""
         _lib.require_cuda(x)
         if self.qkv is not None:
-            q, k, v = _apply_linear(self.qkv, self.n1(x)).chunk(3, dim=-1)
+            q, k, v = _apply_linear(self.qkv, _apply_norm(self.n1, x)).chunk(3, dim=-1)
             a = F.scaled_dot_product_attention(self._split(q), self._split(k), self._split(v))
             x = _apply_linear(self.proj, self._merge(a), residual=x)
-        q = self._split(_apply_linear(self.q_c, self.nx(x)))
+        q = self._split(_apply_linear(self.q_c, _apply_norm(self.nx, x)))
         a = F.scaled_dot_product_attention(q, kv_c[0], kv_c[1])
         x = _apply_linear(self.out_c, self._merge(a), residual=x)
-        return _apply_linear(self.mlp[2], _apply_linear(self.mlp[0], self.n2(x), gelu=True), residual=x)
+        return _apply_linear(self.mlp[2], _apply_linear(self.mlp[0], _apply_norm(self.n2, x), gelu=True), residual=x)
 
 
 class ActionExpert(nn.Module):
@@ -184,13 +205,14 @@ class ActionExpert(nn.Module):
 
     def forward_layers(self, x_act: torch.Tensor, t: torch.Tensor, prefix_kv):
         """The same velocity computed layer by layer (sm_100a GEMMs with fused
-        GELU / residual epilogues, torch norms and attention between them)."""
+        GELU / residual epilogues, the LayerNorm row kernel and torch attention
+        between them)."""
         x = _apply_linear(self.in_proj, x_act)
         temb = _apply_linear(self.t_proj, timestep_embedding(t, self.cfg.d_model).to(x.dtype))
         x = x + temb[:, None, :]
         for blk, kv in zip(self.blocks, prefix_kv):
             x = blk(x, kv)
-        return _apply_linear(self.out_proj, self.out_norm(x))
+        return _apply_linear(self.out_proj, _apply_norm(self.out_norm, x))
 
     @torch.no_grad()
     def sample(self, prefix: torch.Tensor, steps: int = 10, x0: torch.Tensor | None = None):

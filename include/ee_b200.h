@@ -14,6 +14,7 @@
  *   ee_wq_gemm            kernel/triton_gemm.py:141-164 wq_linear
  *                         (+ the Triton kernels at :75-138 it launches)
  *   ee_wq_gemm_status     device status word of the dequant-GEMM (new)
+ *   ee_layer_norm         kernel/flow_expert.py:51-95 the blocks' nn.LayerNorm
  *   ee_flow_sample        kernel/flow_expert.py:127-137 flow_sample, run as
  *                         one fused launch over kernel/flow_expert.py:117-124
  *                         ActionExpert.forward and :83-95 Block.forward
@@ -111,6 +112,15 @@ int ee_wq_gemm(const void* x, const void* weight, const void* scales, const void
  * itself launched without its planned cluster shape and did no work).
  * Synchronises the device; reset != 0 clears the word afterwards. (new) */
 int ee_wq_gemm_status(int32_t* status, int32_t reset);
+
+/* LayerNorm over the last dimension (kernel/flow_expert.py:51-95, the blocks'
+ * nn.LayerNorm; used by the layer-by-layer path): y[r] = (x[r] - mean) *
+ * rsqrt(var + eps) * weight + bias for rows r < rows of `cols` act-dtype
+ * values (row strides ldx / ldy elements), fp32 statistics, one rounding.
+ * weight / bias may be NULL (1 / 0). cols % 8 == 0 and cols <= 2048;
+ * 16-byte aligned pointers and strides. */
+int ee_layer_norm(const void* x, const void* weight, const void* bias, void* y, int64_t rows, int64_t cols,
+                  int64_t ldx, int64_t ldy, float eps, int32_t act_dtype, ee_stream_t stream);
 
 /* ---- fused flow-matching sampler --------------------------------------- */
 typedef struct ee_linear {
