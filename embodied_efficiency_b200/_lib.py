@@ -72,6 +72,8 @@ SIGNATURES = {
     "ee_wq_gemm_status": (c_int32, [ctypes.POINTER(c_int32), c_int32]),
     "ee_layer_norm": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                                 c_float, c_int32, c_void_p]),
+    "ee_attention": (c_int32, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
+                               c_int32, c_int32, c_int32, c_int32, c_int32, c_int64, c_int64, c_int32, c_void_p]),
     "ee_flow_sample_traced": (c_int32, [ctypes.POINTER(Expert), c_void_p, c_void_p, c_void_p, c_int32,
                                         c_int32, c_void_p, c_size_t, c_void_p, c_void_p]),
     "ee_flow_sample_phases": (c_int32, [ctypes.POINTER(Expert), c_int32]),

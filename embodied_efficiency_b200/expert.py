@@ -98,6 +98,21 @@ def _apply_norm(mod, x):
     return mod(x)
 
 
+def _attention(q, ldq, k, ldk, v, ldv, b: int, h: int, hd: int, n_q: int, n_k: int, q_rows: int, k_rows: int):
+    """Non-causal attention on the sm_100a attention units (``ee_attention``)
+    from row-major q / k / v (head j at column j * hd, row strides in elements,
+    the tensors give pointer, dtype and device); returns the merged-head
+    output [b, n_q, h * hd], or None where the kernel does not apply."""
+    if (q.dtype not in (torch.bfloat16, torch.float16) or not q.is_cuda or hd not in (64, 128) or n_q > 64
+            or any(t.data_ptr() % 16 for t in (q, k, v))):
+        return None
+    out = torch.empty(b, n_q, h * hd, device=q.device, dtype=q.dtype)
+    _lib.check(_lib.load().ee_attention(q.data_ptr(), ldq, k.data_ptr(), ldk, v.data_ptr(), ldv, out.data_ptr(),
+                                        h * hd, b, h, hd, n_q, n_k, q_rows, k_rows, _lib.act_code(q.dtype),
+                                        _lib.stream_ptr(q.device)), "ee_attention")
+    return out
+
+
 def _apply_linear(mod, x, gelu: bool = False, residual=None):
     """A linear of the eager path on the sm_100a GEMM (cuBLAS only for K % 128 != 0),
     with GELU or ``residual +`` fused into the GEMM epilogue (the same roundings
@@ -155,13 +170,29 @@ class Block(nn.Module):
     def forward(self, x: torch.Tensor, kv_c):
         """Eager GPU composition (used only where the fused launch does not apply)."""
         _lib.require_cuda(x)
+        b, n, d = x.shape
+        hd = d // self.h
         if self.qkv is not None:
-            q, k, v = _apply_linear(self.qkv, _apply_norm(self.n1, x)).chunk(3, dim=-1)
-            a = F.scaled_dot_product_attention(self._split(q), self._split(k), self._split(v))
-            x = _apply_linear(self.proj, self._merge(a), residual=x)
-        q = self._split(_apply_linear(self.q_c, _apply_norm(self.nx, x)))
-        a = F.scaled_dot_product_attention(q, kv_c[0], kv_c[1])
-        x = _apply_linear(self.out_c, self._merge(a), residual=x)
+            qkv = _apply_linear(self.qkv, _apply_norm(self.n1, x))
+            a = None
+            if qkv.is_contiguous():
+                a = _attention(qkv, 3 * d, qkv[..., d:], 3 * d, qkv[..., 2 * d:], 3 * d, b, self.h, hd, n, n, n, n)
+            if a is None:
+                q, k, v = qkv.chunk(3, dim=-1)
+                a = self._merge(F.scaled_dot_product_attention(self._split(q), self._split(k), self._split(v)))
+            x = _apply_linear(self.proj, a, residual=x)
+        qc = _apply_linear(self.q_c, _apply_norm(self.nx, x))
+        k, v = kv_c
+        a = None
+        p = k.shape[2]
+        es = k.element_size()
+        if (qc.is_contiguous() and k.dtype == qc.dtype and v.dtype == qc.dtype and k.stride() == (p * 2 * d, hd, 2 * d, 1)
+                and v.stride() == k.stride() and v.data_ptr() - k.data_ptr() == d * es):
+            # the prefix K/V views share one [b, P, 2d] projection output
+            a = _attention(qc, d, k, 2 * d, v, 2 * d, b, self.h, hd, n, p, n, p)
+        if a is None:
+            a = self._merge(F.scaled_dot_product_attention(self._split(qc), k, v))
+        x = _apply_linear(self.out_c, a, residual=x)
         return _apply_linear(self.mlp[2], _apply_linear(self.mlp[0], _apply_norm(self.n2, x), gelu=True), residual=x)
 
 

@@ -15,6 +15,7 @@
  *                         (+ the Triton kernels at :75-138 it launches)
  *   ee_wq_gemm_status     device status word of the dequant-GEMM (new)
  *   ee_layer_norm         kernel/flow_expert.py:51-95 the blocks' nn.LayerNorm
+ *   ee_attention          kernel/flow_expert.py:86, :91 scaled_dot_product_attention
  *   ee_flow_sample        kernel/flow_expert.py:127-137 flow_sample, run as
  *                         one fused launch over kernel/flow_expert.py:117-124
  *                         ActionExpert.forward and :83-95 Block.forward
@@ -121,6 +122,16 @@ int ee_wq_gemm_status(int32_t* status, int32_t reset);
  * 16-byte aligned pointers and strides. */
 int ee_layer_norm(const void* x, const void* weight, const void* bias, void* y, int64_t rows, int64_t cols,
                   int64_t ldx, int64_t ldy, float eps, int32_t act_dtype, ee_stream_t stream);
+
+/* Attention of the layer-by-layer path (kernel/flow_expert.py:86, :91,
+ * F.scaled_dot_product_attention, non-causal): for every batch element b and
+ * head h, out[b rows][h*hd ..] = softmax(q k^T / sqrt(hd)) v with q rows
+ * b * q_rows_per_b .. + n_q (n_q <= 64) and key rows b * k_rows_per_b .. + n_k
+ * of row-major q / k / v (head h at column h * hd; row strides in elements),
+ * output merged [rows][n_heads * hd]. hd 64 or 128; act dtype. */
+int ee_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* out,
+                 int64_t ldo, int32_t batch, int32_t n_heads, int32_t head_dim, int32_t n_q, int32_t n_k,
+                 int64_t q_rows_per_b, int64_t k_rows_per_b, int32_t act_dtype, ee_stream_t stream);
 
 /* ---- fused flow-matching sampler --------------------------------------- */
 typedef struct ee_linear {
