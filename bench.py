@@ -288,7 +288,9 @@ def profile_case(spec, launches):
     """A few launches of one kernel for a profiler (no timing, no JSON):
     ``gemm:M:K:BITS`` runs the standalone dequant-GEMM on a square K=N weight,
     ``sampler:BITS`` replays the captured sampler call (a plain cluster launch
-    inside a CUDA graph)."""
+    inside a CUDA graph), ``norm:ROWS:COLS`` runs the LayerNorm row kernel and
+    ``attn:BATCH:P`` the layer path's cross-attention of BATCH requests (50
+    queries, 16 heads of 64, P prefix keys)."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     kind, *rest = spec.split(":")
@@ -324,6 +326,33 @@ def profile_case(spec, launches):
         if gs.status() != 0:
             raise RuntimeError(f"sampler status {gs.status()}")
         print(f"sampler bits={bits} mean|x|={float(y.float().abs().mean()):.5f}")
+    elif kind == "norm":
+        from embodied_efficiency_b200.expert import _apply_norm
+        rows, cols = (int(v) for v in rest)
+        g = torch.Generator(device="cpu").manual_seed(0)
+        x = torch.randn(rows, cols, generator=g).bfloat16().to(dev)
+        ln = torch.nn.LayerNorm(cols).to(dev).bfloat16()
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        with torch.no_grad():
+            for _ in range(launches):
+                flush.zero_()
+                y = _apply_norm(ln, x)
+        torch.cuda.synchronize()
+        print(f"norm rows={rows} cols={cols} mean|y|={float(y.float().abs().mean()):.5f}")
+    elif kind == "attn":
+        from embodied_efficiency_b200.expert import _attention
+        b, p = (int(v) for v in rest)
+        h, hd, n = 16, 64, 50
+        d = h * hd
+        g = torch.Generator(device="cpu").manual_seed(0)
+        q = torch.randn(b, n, d, generator=g).bfloat16().to(dev)
+        kv = torch.randn(b, p, 2 * d, generator=g).bfloat16().to(dev)
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        for _ in range(launches):
+            flush.zero_()
+            y = _attention(q, d, kv, 2 * d, kv[..., d:], 2 * d, b, h, hd, n, p, n, p)
+        torch.cuda.synchronize()
+        print(f"attn batch={b} P={p} mean|y|={float(y.float().abs().mean()):.5f}")
     else:
         raise SystemExit(f"unknown --profile case {spec!r}")
 
@@ -339,7 +368,7 @@ def main():
     ap.add_argument("--no-fleet", action="store_true")
     ap.add_argument("--fleet-chunk", type=int, default=256)
     ap.add_argument("--profile", default=None,
-                    help="gemm:M:K:BITS or sampler:BITS -- a few launches for a profiler")
+                    help="gemm:M:K:BITS, sampler:BITS, norm:ROWS:COLS or attn:BATCH:P -- a few launches for a profiler")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.profile:
