@@ -77,8 +77,187 @@ struct Attn {
     }
   }
 
+  // Running state of one warp over a unit: its 16 query rows of the output
+  // (fp32, unnormalised), the running max / sum of the two rows a lane holds,
+  // and the Q fragments.
+  struct State {
+    float o[HD / 8][4];
+    float mrow[2], lrow[2];
+    uint32_t qf[HD / 16][4];
+  };
+
+  static EE_DEV void reset(State& sw) {
+#pragma unroll
+    for (int i = 0; i < HD / 8; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sw.o[i][c] = 0.f;
+    sw.mrow[0] = sw.mrow[1] = -INFINITY;
+    sw.lrow[0] = sw.lrow[1] = 0.f;
+  }
+
+  // Q fragments of query tile qt (rows 16 qt ..) from the swizzled Q tile
+  static EE_DEV void load_q(State& sw, uint32_t sQ, int qt, int lane) {
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      const int mi = lane >> 3;
+      const int row = qt * 16 + (mi & 1) * 8 + (lane & 7);
+      ldsm_x4(sQ + off(row, 2 * ks + (mi >> 1)), sw.qf[ks][0], sw.qf[ks][1], sw.qf[ks][2], sw.qf[ks][3]);
+    }
+  }
+
+  // one block of 64 keys (keys 64 kb ..; those past n_k are masked) from the
+  // swizzled K / V tiles at kt / vt: S = Q K^T, online softmax, O += P V
+  static EE_DEV void block(State& sw, const AttnArgs& a, uint32_t kt, uint32_t vt, int kb, int lane) {
+    const int t = lane & 3;
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[j][c] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        const int mi = lane >> 3;
+        const int key = 16 * np + (mi >> 1) * 8 + (lane & 7);
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4(kt + off(key, 2 * ks + (mi & 1)), r0, r1, r2, r3);
+        mma16816<T>(s[2 * np], sw.qf[ks][0], sw.qf[ks][1], sw.qf[ks][2], sw.qf[ks][3], r0, r1);
+        mma16816<T>(s[2 * np + 1], sw.qf[ks][0], sw.qf[ks][1], sw.qf[ks][2], sw.qf[ks][3], r2, r3);
+      }
+    }
+    // scale to log2 domain, mask keys past n_k, online softmax
+    const int kbase = kb * 64;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int key = kbase + 8 * j + 2 * t + (c & 1);
+        const float vv = key < a.n_k ? s[j][c] * a.scale_log2 : -INFINITY;
+        s[j][c] = vv;
+        mx[c >> 1] = fmaxf(mx[c >> 1], vv);
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+    }
+    float mnew[2], corr[2], ls[2] = {0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mnew[r] = fmaxf(sw.mrow[r], mx[r]);
+      corr[r] = exp2f(sw.mrow[r] - mnew[r]);
+      sw.mrow[r] = mnew[r];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float p = exp2f(s[j][c] - mnew[c >> 1]);
+        s[j][c] = p;
+        ls[c >> 1] += p;
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 1);
+      ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 2);
+      sw.lrow[r] = sw.lrow[r] * corr[r] + ls[r];
+    }
+#pragma unroll
+    for (int i = 0; i < HD / 8; ++i) {
+      sw.o[i][0] *= corr[0];
+      sw.o[i][1] *= corr[0];
+      sw.o[i][2] *= corr[1];
+      sw.o[i][3] *= corr[1];
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint32_t pa0 = Act<T>::pack2(s[2 * kk][0], s[2 * kk][1]);
+      const uint32_t pa1 = Act<T>::pack2(s[2 * kk][2], s[2 * kk][3]);
+      const uint32_t pa2 = Act<T>::pack2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      const uint32_t pa3 = Act<T>::pack2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int nn = 0; nn < HD / 16; ++nn) {
+        const int mi = lane >> 3;
+        const int key = 16 * kk + (mi & 1) * 8 + (lane & 7);
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4_t(vt + off(key, 2 * nn + (mi >> 1)), r0, r1, r2, r3);
+        mma16816<T>(sw.o[2 * nn], pa0, pa1, pa2, pa3, r0, r1);
+        mma16816<T>(sw.o[2 * nn + 1], pa0, pa1, pa2, pa3, r2, r3);
+      }
+    }
+  }
+
+  // Merge the two key groups (warps 4-7 publish (max, sum, O) through the
+  // merge area, warps 0-3 combine) and store the unit's rows: queries at
+  // rows qr0 .., columns col .. of the output. Contains one __syncthreads;
+  // the merge area is free again after the caller's next one.
+  static EE_DEV void finish(const State& sw, const AttnArgs& a, char* merge, long long qr0, long long col, int warp,
+                            int lane) {
+    const int qt = warp & 3, kg = warp >> 2, g = lane >> 2, t = lane & 3;
+    float* mg = reinterpret_cast<float*>(merge) + (size_t)qt * 16 * (HD + 2);
+    if (kg == 1) {
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int row = g + 8 * r;
+        if (t == 0) {
+          mg[row * (HD + 2) + HD] = sw.mrow[r];
+          mg[row * (HD + 2) + HD + 1] = sw.lrow[r];
+        }
+#pragma unroll
+        for (int i = 0; i < HD / 8; ++i) {
+          mg[row * (HD + 2) + 8 * i + 2 * t] = sw.o[i][2 * r];
+          mg[row * (HD + 2) + 8 * i + 2 * t + 1] = sw.o[i][2 * r + 1];
+        }
+      }
+    }
+    __syncthreads();
+    if (kg == 0) {
+      T* out = reinterpret_cast<T*>(a.out);
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int row = g + 8 * r;
+        const float m1 = mg[row * (HD + 2) + HD], l1 = mg[row * (HD + 2) + HD + 1];
+        const float m = fmaxf(sw.mrow[r], m1);
+        const float c0 = exp2f(sw.mrow[r] - m), c1 = exp2f(m1 - m);
+        const float inv = 1.0f / (sw.lrow[r] * c0 + l1 * c1);
+        const int qi = qt * 16 + row;
+        if (qi < a.n_q) {
+          T* orow = out + (qr0 + qi) * a.ldo + col;
+#pragma unroll
+          for (int i = 0; i < HD / 8; ++i) {
+            const float y0 = (sw.o[i][2 * r] * c0 + mg[row * (HD + 2) + 8 * i + 2 * t] * c1) * inv;
+            const float y1 = (sw.o[i][2 * r + 1] * c0 + mg[row * (HD + 2) + 8 * i + 2 * t + 1] * c1) * inv;
+            *reinterpret_cast<uint32_t*>(orow + 8 * i + 2 * t) = Act<T>::pack2(y0, y1);
+          }
+        }
+      }
+    }
+  }
+
+  // Store a unit computed by one key group alone (every key block in this
+  // warp's state): rows qr0 .., columns col .. of the output.
+  static EE_DEV void store_solo(const State& sw, const AttnArgs& a, long long qr0, long long col, int qt, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    T* out = reinterpret_cast<T*>(a.out);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int qi = qt * 16 + g + 8 * r;
+      const float inv = 1.0f / sw.lrow[r];
+      if (qi < a.n_q) {
+        T* orow = out + (qr0 + qi) * a.ldo + col;
+#pragma unroll
+        for (int i = 0; i < HD / 8; ++i)
+          *reinterpret_cast<uint32_t*>(orow + 8 * i + 2 * t) =
+              Act<T>::pack2(sw.o[i][2 * r] * inv, sw.o[i][2 * r + 1] * inv);
+      }
+    }
+  }
+
   static EE_DEV void unit(const AttnArgs& a, int b, int h, char* smem) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt = warp & 3, kg = warp >> 2;
     const uint32_t sbase = smem_u32(smem);
     const uint32_t sQ = sbase + S::kQ;
@@ -130,14 +309,8 @@ struct Attn {
     load_pair(0, 0);
     cp_async_commit();
 
-    float o[HD / 8][4];
-#pragma unroll
-    for (int i = 0; i < HD / 8; ++i)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) o[i][c] = 0.f;
-    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
-    uint32_t qf[HD / 16][4];
-
+    State sw;
+    reset(sw);
     for (int pi = 0; pi < npairs; ++pi) {
       const int st = pi & 1;
       if (pi + 1 < npairs) load_pair(pi + 1, st ^ 1);
@@ -146,140 +319,13 @@ struct Attn {
       if (tma && !mbar_wait(bar + 8 * st, (uint32_t)((pi >> 1) & 1), a.timeout_ns) && a.status)
         atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
       __syncthreads();
-      if (pi == 0) {
-#pragma unroll
-        for (int ks = 0; ks < HD / 16; ++ks) {
-          const int mi = lane >> 3;
-          const int row = qt * 16 + (mi & 1) * 8 + (lane & 7);
-          ldsm_x4(sQ + off(row, 2 * ks + (mi >> 1)), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
-        }
-      }
+      if (pi == 0) load_q(sw, sQ, qt, lane);
       const int kb = 2 * pi + kg;
-      if (kb < nkb) {
-        const uint32_t kt = sK(st, kg), vt = sV(st, kg);
-        float s[8][4];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) s[j][c] = 0.f;
-#pragma unroll
-        for (int ks = 0; ks < HD / 16; ++ks) {
-#pragma unroll
-          for (int np = 0; np < 4; ++np) {
-            const int mi = lane >> 3;
-            const int key = 16 * np + (mi >> 1) * 8 + (lane & 7);
-            uint32_t r0, r1, r2, r3;
-            ldsm_x4(kt + off(key, 2 * ks + (mi & 1)), r0, r1, r2, r3);
-            mma16816<T>(s[2 * np], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], r0, r1);
-            mma16816<T>(s[2 * np + 1], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], r2, r3);
-          }
-        }
-        // scale to log2 domain, mask keys past n_k, online softmax
-        const int kbase = kb * 64;
-        float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int key = kbase + 8 * j + 2 * t + (c & 1);
-            const float vv = key < a.n_k ? s[j][c] * a.scale_log2 : -INFINITY;
-            s[j][c] = vv;
-            mx[c >> 1] = fmaxf(mx[c >> 1], vv);
-          }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-          mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-        }
-        float mnew[2], corr[2], ls[2] = {0.f, 0.f};
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          mnew[r] = fmaxf(mrow[r], mx[r]);
-          corr[r] = exp2f(mrow[r] - mnew[r]);
-          mrow[r] = mnew[r];
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const float p = exp2f(s[j][c] - mnew[c >> 1]);
-            s[j][c] = p;
-            ls[c >> 1] += p;
-          }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 1);
-          ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 2);
-          lrow[r] = lrow[r] * corr[r] + ls[r];
-        }
-#pragma unroll
-        for (int i = 0; i < HD / 8; ++i) {
-          o[i][0] *= corr[0];
-          o[i][1] *= corr[0];
-          o[i][2] *= corr[1];
-          o[i][3] *= corr[1];
-        }
-        // O += P V
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint32_t pa0 = Act<T>::pack2(s[2 * kk][0], s[2 * kk][1]);
-          const uint32_t pa1 = Act<T>::pack2(s[2 * kk][2], s[2 * kk][3]);
-          const uint32_t pa2 = Act<T>::pack2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-          const uint32_t pa3 = Act<T>::pack2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-#pragma unroll
-          for (int nn = 0; nn < HD / 16; ++nn) {
-            const int mi = lane >> 3;
-            const int key = 16 * kk + (mi & 1) * 8 + (lane & 7);
-            uint32_t r0, r1, r2, r3;
-            ldsm_x4_t(vt + off(key, 2 * nn + (mi >> 1)), r0, r1, r2, r3);
-            mma16816<T>(o[2 * nn], pa0, pa1, pa2, pa3, r0, r1);
-            mma16816<T>(o[2 * nn + 1], pa0, pa1, pa2, pa3, r2, r3);
-          }
-        }
-      }
+      if (kb < nkb) block(sw, a, sK(st, kg), sV(st, kg), kb, lane);
       __syncthreads();  // buffer st is refilled by the next iteration's prefetch
     }
     cp_async_wait<0>();
-
-    // merge the two key groups: group 1 publishes, group 0 combines and stores
-    float* mg = reinterpret_cast<float*>(smem + S::kMerge) + (size_t)qt * 16 * (HD + 2);
-    if (kg == 1) {
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int row = g + 8 * r;
-        if (t == 0) {
-          mg[row * (HD + 2) + HD] = mrow[r];
-          mg[row * (HD + 2) + HD + 1] = lrow[r];
-        }
-#pragma unroll
-        for (int i = 0; i < HD / 8; ++i) {
-          mg[row * (HD + 2) + 8 * i + 2 * t] = o[i][2 * r];
-          mg[row * (HD + 2) + 8 * i + 2 * t + 1] = o[i][2 * r + 1];
-        }
-      }
-    }
-    __syncthreads();
-    if (kg == 0) {
-      T* out = reinterpret_cast<T*>(a.out);
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int row = g + 8 * r;
-        const float m1 = mg[row * (HD + 2) + HD], l1 = mg[row * (HD + 2) + HD + 1];
-        const float m = fmaxf(mrow[r], m1);
-        const float c0 = exp2f(mrow[r] - m), c1 = exp2f(m1 - m);
-        const float inv = 1.0f / (lrow[r] * c0 + l1 * c1);
-        const int qi = qt * 16 + row;
-        if (qi < a.n_q) {
-          T* orow = out + (qr0 + qi) * a.ldo + col;
-#pragma unroll
-          for (int i = 0; i < HD / 8; ++i) {
-            const float y0 = (o[i][2 * r] * c0 + mg[row * (HD + 2) + 8 * i + 2 * t] * c1) * inv;
-            const float y1 = (o[i][2 * r + 1] * c0 + mg[row * (HD + 2) + 8 * i + 2 * t + 1] * c1) * inv;
-            *reinterpret_cast<uint32_t*>(orow + 8 * i + 2 * t) = Act<T>::pack2(y0, y1);
-          }
-        }
-      }
-    }
+    finish(sw, a, smem + S::kMerge, qr0, col, warp, lane);
     __syncthreads();  // smem reuse by the next unit / phase
   }
 };

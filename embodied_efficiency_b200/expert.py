@@ -236,8 +236,8 @@ class ActionExpert(nn.Module):
 
     def forward_layers(self, x_act: torch.Tensor, t: torch.Tensor, prefix_kv):
         """The same velocity computed layer by layer (sm_100a GEMMs with fused
-        GELU / residual epilogues, the LayerNorm row kernel and torch attention
-        between them)."""
+        GELU / residual epilogues, the LayerNorm row kernel and the attention
+        launch between them)."""
         x = _apply_linear(self.in_proj, x_act)
         temb = _apply_linear(self.t_proj, timestep_embedding(t, self.cfg.d_model).to(x.dtype))
         x = x + temb[:, None, :]

@@ -19,7 +19,7 @@ def _ln(x, w, b, eps):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("rows,cols", [(12800, 1024), (3, 256), (1001, 2048), (50, 8)])
+@pytest.mark.parametrize("rows,cols", [(12800, 1024), (3, 256), (1001, 2048), (50, 8), (40000, 512), (777, 1000)])
 def test_matches_torch_layer_norm(cuda, dtype, rows, cols):
     g = torch.Generator(device="cpu").manual_seed(rows + cols)
     x = (torch.randn(rows, cols, generator=g) * 3 + 0.5).to(cuda, dtype)
