@@ -70,6 +70,8 @@ SIGNATURES = {
                                  c_int32, c_void_p, c_size_t, c_void_p]),
     "ee_read_status": (c_int32, [c_void_p, ctypes.POINTER(c_int32), c_void_p]),
     "ee_wq_gemm_status": (c_int32, [ctypes.POINTER(c_int32), c_int32]),
+    "ee_dequant_weight": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32,
+                                    c_int32, c_int32, c_void_p]),
     "ee_layer_norm": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                                 c_float, c_int32, c_void_p]),
     "ee_attention": (c_int32, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,

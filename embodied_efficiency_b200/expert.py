@@ -121,8 +121,7 @@ def _apply_linear(mod, x, gelu: bool = False, residual=None):
     if isinstance(mod, nn.Linear) and mod.in_features % 128 == 0 and fast:
         return wq_linear(x, mod.weight, None, mod.bias, 0, 16, gelu=gelu, residual=residual)
     if type(mod).__name__ == "TritonQuantLinear" and fast:
-        return wq_linear(x, mod.weight, mod.scales, mod.bias, mod.group_size, mod.bits, gelu=gelu,
-                         residual=residual)
+        return mod.linear(x, gelu=gelu, residual=residual)
     y = F.linear(x, mod.weight, mod.bias) if isinstance(mod, nn.Linear) else mod(x)
     if gelu:
         y = F.gelu(y)

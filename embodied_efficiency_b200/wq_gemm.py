@@ -108,6 +108,34 @@ def wq_linear(x, weight, scales, bias, group_size, bits, zeros=None, gelu=False,
     return y.reshape(*lead, n).to(out_dtype)
 
 
+def dequant_weight(weight, scales, group_size, bits, dtype, zeros=None):
+    """[N, K] ``dtype`` (bf16 / fp16) copy of a packed weight, the values the
+    dequant-GEMM multiplies (``ee_dequant_weight``: the exact integer times
+    the scale rounded to ``dtype``, one rounding; kernel/quant.py:33-35)."""
+    _lib.require_cuda(weight, scales)
+    if dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"dequantised weights are bf16 or fp16, not {dtype}")
+    n = weight.shape[0]
+    k = weight.shape[1] * 2 if bits == 4 else weight.shape[1]
+    w = weight.contiguous()
+    s = scales.contiguous()
+    z = None if zeros is None else zeros.to(torch.float16).contiguous()
+    out = torch.empty(n, k, dtype=dtype, device=weight.device)
+    _lib.check(_lib.load().ee_dequant_weight(w.data_ptr(), s.data_ptr(), _lib.ptr(z), out.data_ptr(), n, k,
+                                             wkind_for(bits, z), int(group_size), _lib.act_code(dtype),
+                                             _lib.scale_code(s.dtype), _lib.stream_ptr(weight.device)),
+               "ee_dequant_weight")
+    return out
+
+
+# Tokens from which a quantized linear runs on a cached dense copy of its
+# weight: there the GEMM is bound by the tensor cores, and the tcgen05 kernel
+# with the dense weight brought by TMA straight into the MMA's tiles beats
+# dequantising a weight tile again for every token tile (12800 tokens,
+# K = N = 1024: 40 vs 49 us; K = 4096, N = 1024: 102 vs 137 us).
+DENSE_MIN_TOKENS = 1024
+
+
 def gemm_status(reset: bool = False) -> int:
     """Device status word of the dequant-GEMM kernels on the current device
     (0, or the first error a launch recorded: a bounded in-kernel wait that
@@ -147,8 +175,35 @@ class TritonQuantLinear(nn.Module):
         self.bits, self.group_size = bits, gs
         self.out_features, self.in_features = out, ng * g
 
+    def _dense_key(self, dtype):
+        return (dtype, self.weight.data_ptr(), self.weight._version, self.scales.data_ptr(), self.scales._version)
+
+    def dense_weight(self, dtype):
+        """The weight dequantised into ``dtype`` (``dequant_weight``), made on
+        first use and kept until the weight or scales change; a plain
+        attribute, not a buffer, so ``state_dict`` holds only the packed form."""
+        cached = self.__dict__.get("_dense")
+        if cached is None or cached[0] != self._dense_key(dtype):
+            cached = (self._dense_key(dtype), dequant_weight(self.weight, self.scales, self.group_size, self.bits,
+                                                             dtype))
+            self.__dict__["_dense"] = cached
+        return cached[1]
+
+    def linear(self, x, gelu=False, residual=None):
+        """``wq_linear`` with this module's buffers (and the fused epilogues);
+        from ``DENSE_MIN_TOKENS`` bf16 / fp16 tokens on, on the dense copy of
+        the weight -- the same products, so the same results up to the
+        GEMM's accumulation order. Never builds the copy during stream capture."""
+        m = x.numel() // self.in_features if self.in_features else 0
+        if (x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and m >= DENSE_MIN_TOKENS
+                and (not torch.cuda.is_current_stream_capturing()
+                     or self.__dict__.get("_dense", (None,))[0] == self._dense_key(x.dtype))):
+            return wq_linear(x, self.dense_weight(x.dtype), None, self.bias, 0, 16, gelu=gelu, residual=residual)
+        return wq_linear(x, self.weight, self.scales, self.bias, self.group_size, self.bits, gelu=gelu,
+                         residual=residual)
+
     def forward(self, x):
-        return wq_linear(x, self.weight, self.scales, self.bias, self.group_size, self.bits)
+        return self.linear(x)
 
     def weight_bytes(self) -> float:
         """kernel/quant.py:58-59: int weights + scales counted as fp16."""

@@ -14,6 +14,8 @@
  *   ee_wq_gemm            kernel/triton_gemm.py:141-164 wq_linear
  *                         (+ the Triton kernels at :75-138 it launches)
  *   ee_wq_gemm_status     device status word of the dequant-GEMM (new)
+ *   ee_dequant_weight     kernel/quant.py:33-35 dequantize_weight, with the
+ *                         GEMM's rounding (kernel/triton_gemm.py:91-94, :127-134)
  *   ee_layer_norm         kernel/flow_expert.py:51-95 the blocks' nn.LayerNorm
  *   ee_attention          kernel/flow_expert.py:86, :91 scaled_dot_product_attention
  *   ee_flow_sample        kernel/flow_expert.py:127-137 flow_sample, run as
@@ -113,6 +115,19 @@ int ee_wq_gemm(const void* x, const void* weight, const void* scales, const void
  * itself launched without its planned cluster shape and did no work).
  * Synchronises the device; reset != 0 clears the word afterwards. (new) */
 int ee_wq_gemm_status(int32_t* status, int32_t reset);
+
+/* A packed weight dequantised into the activation dtype (kernel/quant.py:33-35
+ * dequantize_weight; the values are those the dequant-GEMM kernels multiply:
+ * the exact integer times the scale rounded to the activation type, one
+ * rounding, as kernel/triton_gemm.py:91-94 and :127-134 compute them):
+ *   weight  [n, k] int8 (EE_W_INT8) or [n, k/2] packed int4 (EE_W_INT4,
+ *           EE_W_UINT4Z), 16-byte aligned
+ *   scales / zeros / group / scale_dtype as for ee_wq_gemm
+ *   out     [n, k] act dtype, 16-byte aligned
+ * k % 128 == 0, group % 128 == 0 or group == k. Used to cache a dense copy of
+ * a weight for GEMMs with many tokens, where the tensor cores bound the GEMM. */
+int ee_dequant_weight(const void* weight, const void* scales, const void* zeros, void* out, int64_t n, int64_t k,
+                      int32_t wkind, int32_t group, int32_t act_dtype, int32_t scale_dtype, ee_stream_t stream);
 
 /* LayerNorm over the last dimension (kernel/flow_expert.py:51-95, the blocks'
  * nn.LayerNorm; used by the layer-by-layer path): y[r] = (x[r] - mean) *

@@ -226,6 +226,64 @@ def test_quant_linear_module(cuda):
         assert ql.scales.dtype == torch.float32 and ql.scales.shape == (768, 8)
 
 
+@pytest.mark.parametrize("act", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("kind,group", [("int8", 1024), ("int8", 128), ("int4", 128), ("int4z", 128)])
+def test_dequant_weight_bit_exact(cuda, kind, group, act):
+    """ee_dequant_weight against the oracle's dequantisation with the GEMM's
+    rounding: the exact integer times the scale rounded to the activation
+    type, one rounding (zero-point form: v - z, exact, then times the scale)."""
+    from embodied_efficiency_b200.wq_gemm import dequant_weight
+    rng = np.random.default_rng(7)
+    n, k = 384, 1024
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    kt, _ = _quant(w, kind, group)
+    z = None if kt["zeros"] is None else kt["zeros"].to(cuda)
+    got = dequant_weight(kt["weight"].to(cuda), kt["scales"].to(cuda), kt["group"], kt["bits"], act, zeros=z)
+    assert got.shape == (n, k) and got.dtype == act
+    rnd = OQ.round_bf16 if act == torch.bfloat16 else OQ.round_f16
+    gs = kt["group"]
+    ng = k // gs
+    s = rnd(kt["scales"].numpy().astype(np.float32)).reshape(n, ng, 1)
+    if kind == "int4z":
+        v = OQ.unpack_uint4(kt["weight"].numpy()).astype(np.float32)
+        v = v.reshape(n, ng, gs) - kt["zeros"].numpy().astype(np.float32).reshape(n, ng, 1)
+    else:
+        wt = kt["weight"].numpy()
+        v = (OQ.unpack_int4(wt) if kt["bits"] == 4 else wt).astype(np.float32).reshape(n, ng, gs)
+    ref = rnd(v * s).reshape(n, k)
+    assert np.array_equal(got.float().cpu().numpy(), ref)
+
+
+def test_quant_linear_dense_copy_for_many_tokens(cuda):
+    """From DENSE_MIN_TOKENS tokens on, TritonQuantLinear runs on a cached
+    dense copy of its weight: the same result within the GEMM tolerance, one
+    copy reused across calls, rebuilt when the weight changes, and kept out
+    of state_dict."""
+    from embodied_efficiency_b200 import TritonQuantLinear
+    from embodied_efficiency_b200.wq_gemm import DENSE_MIN_TOKENS
+    torch.manual_seed(3)
+    lin = torch.nn.Linear(1024, 1024).to(cuda).bfloat16()
+    x = torch.randn(DENSE_MIN_TOKENS + 77, 1024, device=cuda, dtype=torch.bfloat16)
+    for bits in (8, 4):
+        ql = TritonQuantLinear(lin, bits).to(cuda)
+        with torch.no_grad():
+            y = ql(x)
+            dense = ql.__dict__["_dense"][1]
+            y2 = ql(x)
+        assert ql.__dict__["_dense"][1] is dense
+        assert torch.equal(y, y2)
+        packed = ql.linear(x[:DENSE_MIN_TOKENS - 1])  # below the threshold: the packed weights
+        assert rel_err(y[:DENSE_MIN_TOKENS - 1].float().cpu().numpy(), packed.float().cpu().numpy()) <= TOL
+        ref = torch.nn.functional.linear(x.float(), dense.float(), lin.bias.detach().float())
+        assert rel_err(y.float().cpu().numpy(), ref.cpu().numpy()) <= TOL
+        assert set(ql.state_dict()) == {"weight", "scales", "bias"}
+        with torch.no_grad():
+            ql.scales.mul_(2)
+            y3 = ql(x)
+        assert ql.__dict__["_dense"][1] is not dense
+        assert rel_err(y3.float().cpu().numpy(), (2 * ref - lin.bias.detach().float()).cpu().numpy()) <= TOL
+
+
 def test_zz_gemm_status_clean(cuda):
     """No launch of this module's tests recorded an in-kernel timeout or a
     launch-shape error."""
