@@ -290,7 +290,10 @@ def profile_case(spec, launches):
     ``sampler:BITS`` replays the captured sampler call (a plain cluster launch
     inside a CUDA graph), ``norm:ROWS:COLS`` runs the LayerNorm row kernel and
     ``attn:BATCH:P`` the layer path's cross-attention of BATCH requests (50
-    queries, 16 heads of 64, P prefix keys)."""
+    queries, 16 heads of 64, P prefix keys), ``selfattn:BATCH`` its
+    self-attention over the 50 action tokens (q / k / v read in place from the
+    fused projection) and ``dequant:N:K:BITS`` the weight dequantisation
+    kernel on an [N, K] weight (group 128)."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     kind, *rest = spec.split(":")
@@ -353,6 +356,33 @@ def profile_case(spec, launches):
             y = _attention(q, d, kv, 2 * d, kv[..., d:], 2 * d, b, h, hd, n, p, n, p)
         torch.cuda.synchronize()
         print(f"attn batch={b} P={p} mean|y|={float(y.float().abs().mean()):.5f}")
+    elif kind == "selfattn":
+        from embodied_efficiency_b200.expert import _attention
+        b = int(rest[0])
+        h, hd, n = 16, 64, 50
+        d = h * hd
+        g = torch.Generator(device="cpu").manual_seed(0)
+        qkv = torch.randn(b, n, 3 * d, generator=g).bfloat16().to(dev)
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        for _ in range(launches):
+            flush.zero_()
+            y = _attention(qkv, 3 * d, qkv[..., d:], 3 * d, qkv[..., 2 * d:], 3 * d, b, h, hd, n, n, n, n)
+        torch.cuda.synchronize()
+        print(f"selfattn batch={b} mean|y|={float(y.float().abs().mean()):.5f}")
+    elif kind == "dequant":
+        from embodied_efficiency_b200.quant import quantize_weight
+        from embodied_efficiency_b200.wq_gemm import _pack_int4, dequant_weight
+        n, k, bits = (int(v) for v in rest)
+        g = torch.Generator(device="cpu").manual_seed(0)
+        q, s, _ = quantize_weight(torch.randn(n, k, generator=g) * 0.02, bits, 128)
+        q2 = q.reshape(n, k).to(dev)
+        wt, sc = (_pack_int4(q2) if bits == 4 else q2), s.reshape(n, -1).to(dev)
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        for _ in range(launches):
+            flush.zero_()
+            y = dequant_weight(wt, sc, 128, bits, torch.bfloat16)
+        torch.cuda.synchronize()
+        print(f"dequant n={n} k={k} bits={bits} mean|w|={float(y.float().abs().mean()):.6f}")
     else:
         raise SystemExit(f"unknown --profile case {spec!r}")
 
@@ -368,7 +398,7 @@ def main():
     ap.add_argument("--no-fleet", action="store_true")
     ap.add_argument("--fleet-chunk", type=int, default=256)
     ap.add_argument("--profile", default=None,
-                    help="gemm:M:K:BITS, sampler:BITS, norm:ROWS:COLS or attn:BATCH:P -- a few launches for a profiler")
+                    help="gemm:M:K:BITS, sampler:BITS, norm:ROWS:COLS, attn:BATCH:P, selfattn:BATCH or dequant:N:K:BITS -- a few launches for a profiler")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.profile:
