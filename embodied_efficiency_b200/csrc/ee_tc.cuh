@@ -44,7 +44,13 @@ constexpr int kTcProdWarp = kTcDqWarps, kTcMmaWarp = kTcDqWarps + 1;
 constexpr int kTcWarps = kTcDqWarps + 2;
 constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kTcpEpiWarps = 8;  // epilogue warps of the persistent form (ee_tcp.cuh)
-constexpr uint32_t kTcpEpiBytes = (uint32_t)kTcpEpiWarps * 16u * 32u * 2u;  // per warp [16 tokens][32 rows] of 16-bit
+// With dense weights the persistent form's 16 dequantising warps have no
+// work and join its epilogue (six warps per TMEM lane quarter).
+template <int KIND>
+constexpr int tcp_epi_warps() { return KIND == EE_W_DENSE ? kTcpEpiWarps + kTcDqWarps : kTcpEpiWarps; }
+// per epilogue warp a [16 tokens][32 rows] staging tile of 16-bit values
+template <int KIND>
+constexpr uint32_t tcp_epi_bytes() { return (uint32_t)tcp_epi_warps<KIND>() * 16u * 32u * 2u; }
 
 struct TcArgs {
   ee_linear w;
@@ -558,7 +564,7 @@ int tc_launch_k(const GemmArgs& g, const TcShape& sh, int* status, cudaStream_t 
     const uint32_t off_tm = off_bar + 8u * (2u * (uint32_t)ns_ + 2u * (uint32_t)(dq ? na : 1) + 4u);
     const uint32_t off_recv = tc_align(off_tm + 4u, 16u);
     const uint32_t off_sc = tc_align(off_recv + recv, 16u);
-    return (size_t)tc_align(off_sc + scbytes, 16u) + kTcpEpiBytes + 1024;
+    return (size_t)tc_align(off_sc + scbytes, 16u) + tcp_epi_bytes<KIND>() + 1024;
   };
   // as many stages as fit (at most 8, at most the k-blocks)
   int ns = kbc < 8 ? kbc : 8;
@@ -592,7 +598,7 @@ int tc_launch_k(const GemmArgs& g, const TcShape& sh, int* status, cudaStream_t 
   a.off_recv = tc_align(a.off_tm + 4u, 16u);
   a.off_sc = tc_align(a.off_recv + recv, 16u);
   a.off_ep = tc_align(a.off_sc + scbytes, 16u);
-  const size_t smem = (size_t)a.off_ep + kTcpEpiBytes + 1024;
+  const size_t smem = (size_t)a.off_ep + tcp_epi_bytes<KIND>() + 1024;
   if (smem > (size_t)dp->smem_optin) return EE_OK;
   a.status = status;
   a.timeout_ns = 1000000000ull;

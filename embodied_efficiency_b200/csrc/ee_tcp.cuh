@@ -16,7 +16,10 @@
 //                the NT columns each, in 16-token chunks: bias (and GELU) per lane, the
 //                chunk staged through shared memory as [16 tokens][32 rows],
 //                then per lane 16-byte residual loads (one chunk ahead) and
-//                16-byte stores; the buffer is then released to the MMA issuer
+//                16-byte stores; the buffer is then released to the MMA issuer.
+//                With dense weights (nothing to dequantise) warps 0-15 join
+//                them: six warps per quarter, taking its 16-token chunks in
+//                turn (the GELU of a large-batch MLP is issue-bound with two)
 // The weight and activation tiles, the dequantised A layout, the MMA and the
 // epilogue arithmetic are those of wq_tc_kernel, so the two give identical
 // outputs. Every wait is bounded (%globaltimer); a timeout records
@@ -75,7 +78,7 @@ __global__ void __launch_bounds__(kTcpThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_accf + 8u * b, 1);
-      mbar_init(bar_acce + 8u * b, kTcpEpiWarps);  // the epilogue warps
+      mbar_init(bar_acce + 8u * b, tcp_epi_warps<KIND>());  // the epilogue warps
     }
     mbar_fence_init();
   }
@@ -168,12 +171,20 @@ __global__ void __launch_bounds__(kTcpThreads, 1)
       if (!ok) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
     }
     __syncwarp();
-  } else if (warp >= kTcpEpiWarp0) {
-    // ---------------- epilogue: two warps per 32-lane quarter of TMEM ----------------
-    const int q4 = warp & 3;  // warps 18-25 cover quarters 2, 3, 0, 1, 2, 3, 0, 1
-    const int half = (warp - kTcpEpiWarp0) >> 2;  // which half of the columns
-    constexpr int HC = NT >= 32 ? NT / 2 : NT;     // columns per half (a multiple of 16)
-    const int cbeg = half * HC, cend = NT >= 32 ? cbeg + HC : (half == 0 ? NT : 0);
+  } else if (warp >= kTcpEpiWarp0 || !DQ) {
+    // ---------------- epilogue: two (dense weights: six) warps per 32-lane quarter of TMEM ----------------
+    // A warp reads TMEM lanes 32 (warp % 4) ..: warps 18-25 cover quarters
+    // 2, 3, 0, 1, 2, 3, 0, 1 and warps 0-15 quarters 0, 1, 2, 3, 0, ...
+    const int q4 = warp & 3;
+    const int ew = warp >= kTcpEpiWarp0 ? warp - kTcpEpiWarp0 : kTcpEpiWarps + warp;  // epilogue warp index
+    const int jq = ew >> 2;                                  // index among the quarter's warps
+    constexpr int WQ = tcp_epi_warps<KIND>() / 4;            // warps per quarter
+    // 16-token chunks: with two warps per quarter, each takes a contiguous
+    // half of the NT columns; with six, chunks jq, jq + 6, ...
+    constexpr int HC = NT >= 32 ? NT / 2 : NT;
+    const int cbeg = DQ ? jq * HC : 16 * jq;
+    const int cend = DQ ? (NT >= 32 ? cbeg + HC : (jq == 0 ? NT : 0)) : NT;
+    const int cstep = DQ ? 16 : 16 * WQ;
     const int r = 32 * q4 + lane;
     bool ok = true;
     for (int i = 0; i < my_tiles && ok; ++i) {
@@ -187,7 +198,7 @@ __global__ void __launch_bounds__(kTcpThreads, 1)
       // 8 consecutive rows of one token twice: residual added, 16-byte store
       T* out = reinterpret_cast<T*>(a.out);
       const T* res = reinterpret_cast<const T*>(a.resid);
-      const uint32_t stg = sb + a.off_ep + (uint32_t)(warp - kTcpEpiWarp0) * (16u * 32u * 2u);
+      const uint32_t stg = sb + a.off_ep + (uint32_t)ew * (16u * 32u * 2u);
       const bool vec = (a.ldo % 8) == 0 && (L.n % 8) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
                        (a.epi != EPI_RESID || ((a.ldr % 8) == 0 && (reinterpret_cast<uintptr_t>(a.resid) & 15) == 0));
       const bool vres = vec && a.epi == EPI_RESID;
@@ -210,8 +221,8 @@ __global__ void __launch_bounds__(kTcpThreads, 1)
         break;
       }
       tc_fence_after();
-      for (int c0 = cbeg; c0 < cend; c0 += 16) {
-        if (vres && c0 + 16 < cend) load_res(c0 + 16, rq_nxt);
+      for (int c0 = cbeg; c0 < cend; c0 += cstep) {
+        if (vres && c0 + cstep < cend) load_res(c0 + cstep, rq_nxt);
         uint32_t v[16];
         tmem_ld16(tmem + (uint32_t)buf * TMC + ((uint32_t)(32 * q4) << 16) + (uint32_t)c0, v);
         tmem_wait_ld();
