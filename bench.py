@@ -286,7 +286,9 @@ def run_reference(args):
 
 def profile_case(spec, launches):
     """A few launches of one kernel for a profiler (no timing, no JSON):
-    ``gemm:M:K:BITS`` runs the standalone dequant-GEMM on a square K=N weight,
+    ``gemm:M:K:BITS[:N[:gelu]]`` runs the standalone dequant-GEMM on a K x N
+    weight (N = K unless given; BITS 16 = dense bf16), with the GELU epilogue
+    when asked,
     ``sampler:BITS`` replays the captured sampler call (a plain cluster launch
     inside a CUDA graph), ``norm:ROWS:COLS`` runs the LayerNorm row kernel and
     ``attn:BATCH:P`` the layer path's cross-attention of BATCH requests (50
@@ -301,22 +303,24 @@ def profile_case(spec, launches):
         from embodied_efficiency_b200 import wq_linear
         from embodied_efficiency_b200.quant import quantize_weight
         from embodied_efficiency_b200.wq_gemm import _pack_int4
-        m, k, bits = (int(v) for v in rest)
+        m, k, bits = (int(v) for v in rest[:3])
+        n = int(rest[3]) if len(rest) > 3 else k
+        gelu = len(rest) > 4 and rest[4] == "gelu"
         g = torch.Generator(device="cpu").manual_seed(0)
-        w = torch.randn(k, k, generator=g) * 0.02
+        w = torch.randn(n, k, generator=g) * 0.02
         if bits == 16:
             wt, sc = w.bfloat16().to(dev), None
         else:
             q, s, _ = quantize_weight(w, bits, 128)
-            q2 = q.reshape(k, k).to(dev)
-            wt, sc = (_pack_int4(q2) if bits == 4 else q2), s.reshape(k, -1).to(dev)
+            q2 = q.reshape(n, k).to(dev)
+            wt, sc = (_pack_int4(q2) if bits == 4 else q2), s.reshape(n, -1).to(dev)
         x = torch.randn(m, k, generator=g).bfloat16().to(dev)
         flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
         for _ in range(launches):
             flush.zero_()
-            y = wq_linear(x, wt, sc, None, 128, bits)
+            y = wq_linear(x, wt, sc, None, 128, bits, gelu=gelu)
         torch.cuda.synchronize()
-        print(f"gemm m={m} k=n={k} bits={bits} mean|y|={float(y.float().abs().mean()):.5f}")
+        print(f"gemm m={m} k={k} n={n} bits={bits} gelu={gelu} mean|y|={float(y.float().abs().mean()):.5f}")
     elif kind == "sampler":
         from embodied_efficiency_b200 import GraphedSampler
         bits = int(rest[0]) if rest else 4
@@ -398,7 +402,7 @@ def main():
     ap.add_argument("--no-fleet", action="store_true")
     ap.add_argument("--fleet-chunk", type=int, default=256)
     ap.add_argument("--profile", default=None,
-                    help="gemm:M:K:BITS, sampler:BITS, norm:ROWS:COLS, attn:BATCH:P, selfattn:BATCH or dequant:N:K:BITS -- a few launches for a profiler")
+                    help="gemm:M:K:BITS[:N[:gelu]], sampler:BITS, norm:ROWS:COLS, attn:BATCH:P, selfattn:BATCH or dequant:N:K:BITS -- a few launches for a profiler")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.profile:
