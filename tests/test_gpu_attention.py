@@ -22,7 +22,8 @@ def _merge(x):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("b,n,h,hd,p", [(256, 50, 16, 64, 256), (3, 50, 8, 128, 100), (5, 17, 4, 64, 33),
-                                         (41, 64, 16, 64, 64), (7, 50, 16, 64, 700), (300, 50, 8, 128, 50)])
+                                         (41, 64, 16, 64, 64), (7, 50, 16, 64, 700), (300, 50, 8, 128, 50),
+                                         (9, 33, 16, 64, 100), (150, 50, 16, 64, 200)])
 def test_matches_sdpa(cuda, dtype, b, n, h, hd, p):
     from embodied_efficiency_b200.expert import _attention
     g = torch.Generator(device="cpu").manual_seed(b * 7 + p)
