@@ -92,7 +92,7 @@ def test_golden_config1_int8_per_channel(cuda):
     gold = bits_to_f32(g["c1_y"])
     assert rel_err(y, gold) <= TOL
     assert rel_err(y, ref) <= TOL
-    # fp16 scales = max|W_row|/127 stored in half
+    # fp16 scales = max|W_row|/127 stored in half (the single int8 per-channel GEMM workload)
     y16, ref16 = _run(cuda, x, w, "int8", 1024, scale_f16=True)
     assert rel_err(y16, ref16) <= TOL and rel_err(y16, gold) <= TOL
 
