@@ -73,6 +73,19 @@ def test_argument_errors_without_launch(lib):
     a[2] = 16
     a[11] = 96
     assert lib.ee_wq_gemm(*a) == 2                    # group does not divide K
+    # ee_dequant_weight(weight, scales, zeros, out, n, k, wkind, group, act, scale_dtype, stream)
+    dq = [16, 16, 0, 16, 64, 1024, _lib.EE_W_INT4, 128, _lib.EE_BF16, _lib.EE_F32, None]
+    for i, v, rc in ((0, 0, 1),                       # no weight
+                     (8, 7, 4),                       # bad act dtype
+                     (6, _lib.EE_W_DENSE, 1),         # nothing to dequantise
+                     (5, 96, 2),                      # K % 128
+                     (1, 0, 1),                       # int4 needs scales
+                     (3, 8, 3),                       # misaligned output
+                     (7, 96, 2),                      # group does not divide K
+                     (6, _lib.EE_W_UINT4Z, 1)):       # zero-point form needs zeros
+        a = list(dq)
+        a[i] = v
+        assert lib.ee_dequant_weight(*a) == rc, (i, v)
     assert lib.ee_flow_sample(None, 0, 0, 0, 10, 0, 0, 0, None) == 1
     assert lib.ee_barrier_selftest(None, 1000, None) == 1
     assert lib.ee_barrier_selftest(16, 0, None) == 1
