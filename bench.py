@@ -8,12 +8,16 @@ bf16 activations. A "step" of this benchmark is one sampler call (10 Euler
 steps). ``value`` is device time per call with inputs resident in HBM and the
 L2 flushed between calls; ``e2e`` is the same call through ``GraphedSampler``
 with the input in pinned host memory and the result copied back to the host
-inside the timed region. bf16 and int8 weights are reported beside int4, and
-the standalone dequant-GEMM's HBM throughput for the K=N=4096 sweep points.
+inside the timed region. bf16 and int8 weights are reported beside int4; at
+N=1 also the standalone dequant-GEMM's HBM throughput (``gemm``), the prefix
+encoder's kv_c GEMM (``kv_prefix_gemm``), the reference-default expert
+(``config3_ref``) and the Pi0-scale expert (``config5``).
 
 Multi-GPU (torchrun, one rank per GPU): independent replicas of the batch-1
-call (the call does not shard); ``value`` is the job's time per call
-(max-over-ranks device time / calls of all ranks), ``scaling`` "weak".
+call (the call does not shard); ``value`` is the latency of one call, the
+max over ranks of each rank's mean device time per call, ``scaling`` "weak".
+The sharded workload is fleet mode (``fleet``): 256 independent requests
+split over the ranks, aggregate actions/s, measured at every N.
 
 ``--impl reference`` times the CPU restatement of the reference's own path
 (the oracle: dequantise-then-matmul + eager Euler loop in torch on the host
@@ -37,6 +41,10 @@ import torch  # noqa: E402
 WORKLOAD = dict(d_model=1024, n_layers=4, n_heads=16, horizon=50, action_dim=32, prefix_len=256,
                 mlp_ratio=4.0)
 METRIC = "ms per 10-step sampler call (batch 1)"
+# the reference's default expert (kernel/flow_expert.py:28-35), the shape of its published numbers
+CONFIG3_REF = dict(d_model=512, n_layers=6, n_heads=8, horizon=50, action_dim=32, prefix_len=256, mlp_ratio=4.0)
+# the Pi0-scale expert: 18 blocks of width 2048, MLP 8192, 16 heads x 128, prefix 816
+CONFIG5 = dict(d_model=2048, n_layers=18, n_heads=16, horizon=50, action_dim=32, prefix_len=816, mlp_ratio=4.0)
 N_STEPS = 10
 L2_FLUSH_BYTES = 256 << 20
 # DRAM bytes (read + write) of one sampler_kernel launch of WORKLOAD at int4,
@@ -168,29 +176,123 @@ def time_calls(fn, steps, warmup, flush):
     return [a.elapsed_time(b) for a, b in ev]
 
 
-def gemm_sweep(device, flush):
-    """Standalone dequant-GEMM at K=N=4096: algorithmic HBM GB/s per launch."""
-    from embodied_efficiency_b200 import wq_linear
+def _weight_copies(n, k, bits, device, copies, g):
+    """`copies` independent [n, k] weights (packed int4 / int8 + fp32 scales,
+    or bf16), quantised from N(0, 0.02) draws."""
     from embodied_efficiency_b200.quant import quantize_weight
     from embodied_efficiency_b200.wq_gemm import _pack_int4
+    out = []
+    for _ in range(copies):
+        w = torch.randn(n, k, generator=g, device=device) * 0.02
+        if bits == 16:
+            out.append((w.bfloat16(), None))
+        else:
+            q, sc, _ = quantize_weight(w, bits, 128)
+            q2 = q.reshape(n, k)
+            out.append((_pack_int4(q2) if bits == 4 else q2, sc.reshape(n, -1)))
+        del w
+    return out
+
+
+def gemm_sweep(device, shapes=((4096, 4096), (8192, 8192), (6144, 2048), (8192, 2048), (2048, 8192)),
+               ms=(1, 16, 50), bits_list=(4, 8, 16), reps=20):
+    """Standalone dequant-GEMM (``wq_linear``), N x K weights, M tokens:
+    back-to-back launches replayed from one CUDA graph that cycles through
+    enough independent weight copies to exceed twice the L2 (each launch
+    reads its weights from HBM); per-launch time = graph time / launches.
+    Reports algorithmic HBM GB/s (weights + fp16-counted scales +
+    activations + output) and TFLOP/s."""
+    from embodied_efficiency_b200 import wq_linear
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    g = torch.Generator(device=device).manual_seed(0)
     out = {}
-    k = n = 4096
-    g = torch.Generator(device="cpu").manual_seed(0)
-    w = torch.randn(n, k, generator=g) * 0.02
-    mats = {16: (w.bfloat16().to(device), None)}
-    for bits in (8, 4):
-        q, s, gs = quantize_weight(w, bits, 128)
-        q2 = q.reshape(n, k).to(device)
-        mats[bits] = (_pack_int4(q2) if bits == 4 else q2, s.reshape(n, -1).to(device))
-    for m in (1, 16, 50, 128, 512):
-        x = torch.randn(m, k, generator=g).bfloat16().to(device)
-        for bits, (wt, sc) in mats.items():
-            ms = time_calls(lambda: wq_linear(x, wt, sc, None, 128, bits), 50, 5, flush)
-            t = statistics.median(ms)
-            nbytes = linear_bytes(n, k, bits) - n * 2 + m * k * 2 + m * n * 2
-            out[f"m{m}_{'bf16' if bits == 16 else f'int{bits}'}"] = {
-                "us": round(t * 1e3, 2), "GBps": round(nbytes / (t * 1e-3) / 1e9, 1),
-                "TFLOPs": round(2.0 * m * n * k / (t * 1e-3) / 1e12, 1)}
+    for (n, k) in shapes:
+        for bits in bits_list:
+            wbytes = linear_bytes(n, k, bits) - n * 2
+            copies = max(2, min(64, -(-2 * l2 // wbytes)))
+            mats = _weight_copies(n, k, bits, device, copies, g)
+            for m in ms:
+                x = torch.randn(m, k, generator=g, device=device).bfloat16()
+                for wt, sc in mats[:2]:
+                    wq_linear(x, wt, sc, None, 128, bits)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for wt, sc in mats:
+                        wq_linear(x, wt, sc, None, 128, bits)
+                graph.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    graph.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                t = e0.elapsed_time(e1) / (reps * copies)
+                nbytes = wbytes + m * k * 2 + m * n * 2
+                out[f"n{n}_k{k}_m{m}_{'bf16' if bits == 16 else f'int{bits}'}"] = {
+                    "us": round(t * 1e3, 2), "GBps": round(nbytes / (t * 1e-3) / 1e9, 1),
+                    "TFLOPs": round(2.0 * m * n * k / (t * 1e-3) / 1e12, 1)}
+                del graph
+            del mats
+            torch.cuda.empty_cache()
+    return out
+
+
+def sampler_variants(cfg_kw, device, flush, bits_list=(16, 8, 4), calls=20, warmup=5, batch=1):
+    """ms per 10-step call (device time, L2 flushed between calls) of an
+    expert of the given shape at bf16 / int8 / int4 weights, batch ``batch``;
+    weights drawn on the device (not the oracle's seeded set)."""
+    from embodied_efficiency_b200 import ActionExpert, ActionExpertConfig, GraphedSampler, quantize_model_triton
+    cfg = ActionExpertConfig(**cfg_kw)
+    out = {}
+    for bits in bits_list:
+        torch.manual_seed(0)
+        with torch.device(device):
+            m = ActionExpert(cfg)
+        with torch.no_grad():
+            for name, prm in m.named_parameters():
+                if "n1" in name or "nx" in name or "n2" in name or "out_norm" in name:
+                    continue
+                prm.normal_(0.0, 0.02)
+        m = m.bfloat16().eval()
+        if bits != 16:
+            quantize_model_triton(m, bits=bits)
+        g = torch.Generator(device=device).manual_seed(1)
+        x = torch.randn(batch, cfg.horizon, cfg.action_dim, generator=g, device=device).bfloat16()
+        prefix = torch.randn(batch, cfg.prefix_len, cfg.d_model, generator=g, device=device).bfloat16()
+        gs = GraphedSampler(m, x, N_STEPS, warmup=2, prefix_kv=m.encode(prefix))
+        ms = time_calls(gs.replay, calls, warmup, flush)
+        w_b, kv_b = step_bytes(cfg_kw, bits, batch)
+        t = statistics.median(ms)
+        out["bf16" if bits == 16 else f"int{bits}"] = {
+            "ms_per_call": round(t, 4), "weight_MB_per_step": round(w_b / 1e6, 2),
+            "weight_GBps": round(w_b * N_STEPS / (t * 1e-3) / 1e9, 1),
+            "path": "fused launch" if gs.fused else "layer by layer (CUDA graph)"}
+        del gs, m
+        torch.cuda.empty_cache()
+    return out
+
+
+def kv_prefix_gemm(device, flush):
+    """The prefix encoder's kv_c GEMM (kernel/flow_expert.py:78-81, once per
+    call): M = P * batch tokens, N = 2 d, K = d, int4 group-128; device time
+    per launch (L2 flushed), TFLOP/s and algorithmic GB/s."""
+    from embodied_efficiency_b200 import wq_linear
+    g = torch.Generator(device=device).manual_seed(0)
+    out = {}
+    for tag, d, p, b in (("c3_P256_B1", 1024, 256, 1), ("c5_P816_B1", 2048, 816, 1),
+                         ("c5_P816_B8", 2048, 816, 8), ("fleet_P256_B256", 1024, 256, 256)):
+        (wt, sc), = _weight_copies(2 * d, d, 4, device, 1, g)
+        x = torch.randn(p * b, d, generator=g, device=device).bfloat16()
+        ms = time_calls(lambda: wq_linear(x, wt, sc, None, 128, 4), 20, 3, flush)
+        t = statistics.median(ms)
+        m = p * b
+        nbytes = linear_bytes(2 * d, d, 4) + m * d * 2 + m * 2 * d * 2
+        out[tag] = {"M": m, "N": 2 * d, "K": d, "us": round(t * 1e3, 2),
+                    "TFLOPs": round(2.0 * m * 2 * d * d / (t * 1e-3) / 1e12, 1),
+                    "GBps": round(nbytes / (t * 1e-3) / 1e9, 1)}
+        del wt, sc, x
     return out
 
 
@@ -400,6 +502,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-fleet", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the config 3-ref and config 5 sampler lines")
     ap.add_argument("--fleet-chunk", type=int, default=256)
     ap.add_argument("--profile", default=None,
                     help="gemm:M:K:BITS[:N[:gelu]], sampler:BITS, norm:ROWS:COLS, attn:BATCH:P, selfattn:BATCH or dequant:N:K:BITS -- a few launches for a profiler")
@@ -440,7 +543,7 @@ def main():
     if world > 1:
         torch.distributed.all_reduce(t_max, op=torch.distributed.ReduceOp.MAX)
         torch.distributed.barrier()
-    value = t_max.item() / (args.steps * world)
+    value = t_max.item() / args.steps  # one call's latency (max over the replicas)
     status = plan.status(N_STEPS)
     if status != 0:
         raise RuntimeError(f"sampler status {status}")
@@ -458,14 +561,16 @@ def main():
     e2e_total = torch.tensor([sum(e2e_ms)], device=dev)
     if world > 1:
         torch.distributed.all_reduce(e2e_total, op=torch.distributed.ReduceOp.MAX)
-    e2e_value = e2e_total.item() / (args.steps * world)
+    e2e_value = e2e_total.item() / args.steps
 
     fleet = None if args.no_fleet else fleet_run(m, rank, world, dev, chunk=args.fleet_chunk)
 
+    # every rank's GPU work is done; the other ranks leave before rank 0
+    # times the CPU baseline, so no rank spins on the host cores meanwhile
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
     if rank != 0:
-        if world > 1:
-            torch.distributed.barrier()
-            torch.distributed.destroy_process_group()
         return
 
     hbm, peak_kind = peaks()
@@ -506,8 +611,22 @@ def main():
     }
     if fleet is not None:
         line["fleet"] = fleet
-    if not args.no_sweep:
-        line["gemm_k4096"] = gemm_sweep(dev, flush)
+    if world == 1 and not args.no_sweep:
+        line["gemm"] = gemm_sweep(dev)
+        line["gemm_method"] = ("wq_linear back to back in one CUDA graph over weight copies totalling "
+                               ">= 2x L2 (weights from HBM every launch); time per launch")
+        line["kv_prefix_gemm"] = kv_prefix_gemm(dev, flush)
+    if world == 1 and not args.no_extra:
+        line["config3_ref"] = sampler_variants(CONFIG3_REF, dev, flush)
+        line["config3_ref"]["workload"] = ("reference default expert d512 L6 h8x64 mlp2048 P256 H50 A32, "
+                                           "batch 1, 10 steps, CUDA graph; L4 published 4.4709 / 5.9973 / "
+                                           "12.3748 ms bf16 / int8 / int4 (space/app/pareto.py:34-36)")
+        c5 = sampler_variants(CONFIG5, dev, flush, calls=10, warmup=3)
+        for b in (8, 64):
+            c5.update({f"{k}_B{b}": v for k, v in
+                       sampler_variants(CONFIG5, dev, flush, bits_list=(4,), calls=5, warmup=2, batch=b).items()})
+        c5["workload"] = "Pi0-scale expert d2048 L18 h16x128 mlp8192 P816 H50 A32, 10 steps, CUDA graph"
+        line["config5"] = c5
     if not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
         v, n = cpu_baseline_run()
@@ -516,9 +635,6 @@ def main():
                                 "sample": f"{n} full sampler calls of the same workload (oracle "
                                           "restatement of the reference path, torch CPU, bf16)"}
     print(json.dumps(line))
-    if world > 1:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
 
 
 if __name__ == "__main__":

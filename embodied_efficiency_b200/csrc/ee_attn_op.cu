@@ -135,6 +135,8 @@ extern "C" int ee_attention(const void* q, int64_t ldq, const void* k, int64_t l
   if (ldq < hw || ldk < hw || ldv < hw || ldo < hw || (ldq % 8) || (ldk % 8) || (ldv % 8) || (ldo % 2))
     return EE_ERR_SHAPE;
   if (q_rows_per_b < n_q || k_rows_per_b < n_k) return EE_ERR_SHAPE;
+  // the units index rows with 32-bit row counts per batch item
+  if (q_rows_per_b > 0x7fffffffLL || k_rows_per_b > 0x7fffffffLL) return EE_ERR_SHAPE;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (reinterpret_cast<uintptr_t>(out) & 3)) return EE_ERR_ALIGN;
   if (act_dtype != EE_BF16 && act_dtype != EE_F16) return EE_ERR_DTYPE;
   const int rc = check_device();

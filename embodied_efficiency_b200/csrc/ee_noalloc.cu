@@ -23,24 +23,57 @@ constexpr size_t kStaticScratchBytes = 4u << 20;
 
 static __device__ __align__(256) unsigned char g_sampler_scratch[kStaticScratchBytes];
 
+// Identity of the CUDA context current on this thread (0 when the driver
+// cannot tell): cuCtxGetCurrent + cuCtxGetId, looked up from the driver once
+// (no libcuda link).
+typedef int (*CtxGetCurrentFn)(void**);
+typedef int (*CtxGetIdFn)(void*, unsigned long long*);
+static unsigned long long current_context_id() {
+  static std::once_flag once;
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+    cudaGetLastError();
+  });
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != 0 || !ctx || get_id(ctx, &id) != 0) return 0;
+  return id;
+}
+
 // Device address of g_sampler_scratch on the current device, looked up once
-// per device (the symbol's host-side name is not a device address).
+// per device and context (the symbol's host-side name is not a device
+// address). A device whose context was destroyed and made again
+// (cudaDeviceReset) reloads the library's device image, possibly at another
+// address, so the lookup is repeated for the new context.
 static void* scratch_address(int* rc) {
   static std::mutex mu;
   static void* addr[64] = {};
+  static unsigned long long ctx_of[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     *rc = EE_ERR_DEVICE;
     return nullptr;
   }
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> g(mu);
-  if (!addr[dev]) {
+  if (!addr[dev] || ctx != ctx_of[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_sampler_scratch) != cudaSuccess || !p) {
       *rc = EE_ERR_LAUNCH;
       return nullptr;
     }
     addr[dev] = p;
+    ctx_of[dev] = ctx;
   }
   *rc = EE_OK;
   return addr[dev];

@@ -262,10 +262,13 @@ _PLANS: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
 def get_plan(expert, batch: int, prefix_kv):
     """Fused-launch plan of any action-expert module (this package's or the
     reference's) for a batch and prefix K/V, cached on the module and rebuilt
-    when a parameter is replaced or modified in place."""
+    when a parameter or buffer is replaced or modified in place (quantised
+    linears keep their integers and scales in buffers, and a plan packs
+    private copies of them, so ``load_state_dict`` into a quantised model
+    must retire the plan)."""
     key = (batch, tuple(kv[0].data_ptr() for kv in prefix_kv),
            tuple((p.data_ptr(), p._version) for p in expert.parameters()),
-           tuple(b.data_ptr() for b in expert.buffers()))
+           tuple((b.data_ptr(), b._version) for b in expert.buffers()))
     cache = _PLANS.setdefault(expert, {})
     pl = cache.get(key)
     if pl is None:

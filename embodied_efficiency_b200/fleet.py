@@ -6,7 +6,11 @@ the fleet is split into contiguous blocks of requests, one block per rank (one
 process per GPU), with no collective on the data path. Inside a rank the block
 runs as sampler calls over chunks of ``chunk`` requests (every GEMM of a call
 sees 50 * chunk tokens): small chunks as the single fused launch, large ones
-layer by layer on the tcgen05 dequant-GEMM (``flow_sample`` picks).
+layer by layer on the tcgen05 dequant-GEMM (``flow_sample`` picks). On a CUDA
+device each chunk's whole 10-step call is captured once as a CUDA graph
+(``GraphedSampler`` with the chunk's own prefix K/V), so a fleet step replays
+one graph per chunk instead of dispatching every kernel of the layer-by-layer
+path from Python.
 Results come back through host memory; ``gather_results`` assembles the whole
 fleet on one rank over any process group (gloo included) when a caller wants
 it, and is not part of the timed path.
@@ -55,7 +59,7 @@ class FleetSampler:
     """
 
     def __init__(self, n_requests: int, rank: int, world: int, chunk: int = 256, n_steps: int = 10,
-                 expert=None, sample_fn: Optional[Callable] = None, device=None):
+                 expert=None, sample_fn: Optional[Callable] = None, device=None, graphs: bool = True):
         if (expert is None) == (sample_fn is None):
             raise ValueError("give exactly one of expert / sample_fn")
         self.n, self.rank, self.world = n_requests, rank, world
@@ -63,7 +67,9 @@ class FleetSampler:
         self.lo, self.hi = shard_bounds(n_requests, rank, world)
         self.expert, self.sample_fn = expert, sample_fn
         self.device = device
+        self.graphs = graphs
         self._inputs = None
+        self._graphs = None
 
     def stage(self, request_fn: Callable[[int], tuple]):
         """Build this rank's chunks once: per chunk the stacked prefixes and
@@ -82,6 +88,11 @@ class FleetSampler:
                 kv = self.expert.encode(pre)
             staged.append((a, b, pre, x0, kv))
         self._inputs = staged
+        self._graphs = None
+        if self.expert is not None and self.graphs and staged and staged[0][3].is_cuda:
+            from .graphed import GraphedSampler
+            self._graphs = [GraphedSampler(self.expert, x0, self.n_steps, warmup=2, prefix_kv=kv)
+                            for _, _, _, x0, kv in staged]
         return self
 
     def run_device(self) -> list[torch.Tensor]:
@@ -89,6 +100,10 @@ class FleetSampler:
         left on the device (no host synchronisation)."""
         if self._inputs is None:
             raise RuntimeError("stage() the requests first")
+        if self._graphs is not None:
+            # one replay per chunk; each output is the chunk graph's static
+            # buffer, overwritten by its next replay
+            return [g.replay() for g in self._graphs]
         outs = []
         for a, b, pre, x0, kv in self._inputs:
             if self.expert is not None:

@@ -13,20 +13,28 @@ import torch
 
 from . import _lib
 from . import fused as _fused
+from . import expert as _expert
 from .expert import flow_sample, get_plan
 
 
 class GraphedSampler:
     """Captures ``flow_sample(expert, x, n_steps)`` into a CUDA graph with a static input."""
 
-    def __init__(self, expert, x_template, n_steps, warmup=5):
+    def __init__(self, expert, x_template, n_steps, warmup=5, prefix_kv=None):
+        """``prefix_kv`` (not in the reference, whose sampler always encodes
+        the module's own prefix) bakes given per-layer K/V -- requests' own
+        prefixes, as fleet mode has them -- into the graph instead of
+        ``expert.encode_prefix(batch)``."""
         _lib.require_cuda(x_template)
         self.expert, self.n = expert, n_steps
         self.cuda = True
-        self.prefix_kv = expert.encode_prefix(x_template.shape[0])  # constant, baked into the graph
+        # constant, baked into the graph
+        self.prefix_kv = prefix_kv if prefix_kv is not None else expert.encode_prefix(x_template.shape[0])
         self.static_in = x_template.clone()
         b = x_template.shape[0]
-        self.fused = _fused.supports(expert, b)
+        # the same choice flow_sample makes: the single fused launch up to
+        # FUSED_MAX_TOKENS tokens, else the layer-by-layer path (captured too)
+        self.fused = _fused.supports(expert, b) and b * expert.cfg.horizon <= _expert.FUSED_MAX_TOKENS
         self.plan = get_plan(expert, b, self.prefix_kv) if self.fused else None
         if self.fused:
             self.static_out = torch.empty_like(self.static_in, dtype=self.plan.act)
@@ -53,6 +61,12 @@ class GraphedSampler:
         self.static_in.copy_(x)          # never trust the new tensor's address, copy in
         self.graph.replay()
         return self.static_out.to(x.dtype).clone()  # storage is reused on next replay
+
+    def replay(self):
+        """Replay on the input already in ``static_in``; returns ``static_out``
+        itself (overwritten by the next replay, no copy)."""
+        self.graph.replay()
+        return self.static_out
 
     def status(self) -> int:
         """Device status word of the last replay (synchronises); 0 = ok."""

@@ -68,6 +68,36 @@ def wkind_for(bits: int, zeros=None) -> int:
     raise ValueError(f"bits must be 4, 8 or 16, got {bits}")
 
 
+def _check_quant_operands(weight, scales, zeros, n, k, group_size, bits):
+    """Shape / dtype / device checks the C ABI cannot make (it sees raw
+    pointers): scales (and zero points) must be [n, k / group_size] on the
+    weight's device, or the kernels would read past their end."""
+    if bits == 16:
+        return
+    if scales is None:
+        raise ValueError(f"int{bits} weights need scales")
+    g = int(group_size)
+    if g <= 0 or k % g:
+        raise ValueError(f"group_size {group_size} does not divide K={k}")
+    if tuple(scales.shape) != (n, k // g):
+        raise ValueError(f"scales have shape {tuple(scales.shape)}, expected {(n, k // g)} "
+                         f"for a [{n}, {k}] weight with group_size {g}")
+    if scales.dtype not in (torch.float32, torch.float16):
+        raise ValueError(f"scales must be float32 or float16, not {scales.dtype}")
+    if scales.device != weight.device:
+        raise ValueError("scales and weight are on different devices")
+    if zeros is not None:
+        if tuple(zeros.shape) != (n, k // g):
+            raise ValueError(f"zeros have shape {tuple(zeros.shape)}, expected {(n, k // g)}")
+        if zeros.device != weight.device:
+            raise ValueError("zeros and weight are on different devices")
+        if bits != 4:
+            raise ValueError("zero points apply to int4 weights only")
+    ok = (torch.uint8, torch.int8) if bits == 4 else (torch.int8,)
+    if weight.dtype not in ok:
+        raise ValueError(f"int{bits} weights are {' or '.join(map(str, ok))}, not {weight.dtype}")
+
+
 def wq_linear(x, weight, scales, bias, group_size, bits, zeros=None, gelu=False, residual=None):
     """kernel/triton_gemm.py:141-164: ``x @ dequant(weight).T + bias`` in x.dtype.
 
@@ -78,12 +108,15 @@ def wq_linear(x, weight, scales, bias, group_size, bits, zeros=None, gelu=False,
     ``residual`` (+ residual, both rounded as separate torch ops would).
     ``bits=16`` means ``weight`` is a dense [N, K] matrix in the activation dtype.
     """
-    _lib.require_cuda(x, weight)
+    if bits not in (4, 8, 16):
+        raise ValueError(f"bits must be 4, 8 or 16, got {bits}")
     *lead, k_in = x.shape
     n = weight.shape[0]
     k = weight.shape[1] * 2 if bits == 4 else weight.shape[1]
     if k_in != k:
         raise ValueError(f"x has K={k_in}, weight has K={k}")
+    _check_quant_operands(weight, scales, zeros, n, k, group_size, bits)
+    _lib.require_cuda(x, weight)
     out_dtype = x.dtype
     act = x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
     xf = x.reshape(-1, k).to(act).contiguous()
@@ -112,11 +145,14 @@ def dequant_weight(weight, scales, group_size, bits, dtype, zeros=None):
     """[N, K] ``dtype`` (bf16 / fp16) copy of a packed weight, the values the
     dequant-GEMM multiplies (``ee_dequant_weight``: the exact integer times
     the scale rounded to ``dtype``, one rounding; kernel/quant.py:33-35)."""
-    _lib.require_cuda(weight, scales)
     if dtype not in (torch.bfloat16, torch.float16):
         raise ValueError(f"dequantised weights are bf16 or fp16, not {dtype}")
+    if bits not in (4, 8):
+        raise ValueError(f"bits must be 4 or 8, got {bits}")
     n = weight.shape[0]
     k = weight.shape[1] * 2 if bits == 4 else weight.shape[1]
+    _check_quant_operands(weight, scales, zeros, n, k, group_size, bits)
+    _lib.require_cuda(weight, scales)
     w = weight.contiguous()
     s = scales.contiguous()
     z = None if zeros is None else zeros.to(torch.float16).contiguous()
@@ -132,7 +168,10 @@ def dequant_weight(weight, scales, group_size, bits, dtype, zeros=None):
 # weight: there the GEMM is bound by the tensor cores, and the tcgen05 kernel
 # with the dense weight brought by TMA straight into the MMA's tiles beats
 # dequantising a weight tile again for every token tile (12800 tokens,
-# K = N = 1024: 40 vs 49 us; K = 4096, N = 1024: 102 vs 137 us).
+# K = N = 1024: 40 vs 49 us; K = 4096, N = 1024: 102 vs 137 us). The copy
+# costs device memory for as long as the module lives: 2 bytes per weight
+# (4x the packed int4 bytes, 2x int8), about 2.2 GB for a 1.1 B-weight
+# model. None turns the copy off (every call then runs on the packed weight).
 DENSE_MIN_TOKENS = 1024
 
 
@@ -195,7 +234,8 @@ class TritonQuantLinear(nn.Module):
         the weight -- the same products, so the same results up to the
         GEMM's accumulation order. Never builds the copy during stream capture."""
         m = x.numel() // self.in_features if self.in_features else 0
-        if (x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and m >= DENSE_MIN_TOKENS
+        if (DENSE_MIN_TOKENS is not None and x.is_cuda and x.dtype in (torch.bfloat16, torch.float16)
+                and m >= DENSE_MIN_TOKENS
                 and (not torch.cuda.is_current_stream_capturing()
                      or self.__dict__.get("_dense", (None,))[0] == self._dense_key(x.dtype))):
             return wq_linear(x, self.dense_weight(x.dtype), None, self.bias, 0, 16, gelu=gelu, residual=residual)

@@ -252,7 +252,10 @@ int ee_flow_sample_geometry(const ee_expert* ex, int32_t* grid_ctas, int32_t* cl
  *     EE_ERR_WORKSPACE and launch nothing.
  *   - Allocates nothing: no cudaMalloc / cudaFree, no allocating library call.
  *   - The first call on a device looks up the array's device address; make
- *     that first call before any stream capture on that device.
+ *     that first call before any stream capture on that device. The lookup
+ *     is repeated when the device's context has been destroyed and made
+ *     again (cudaDeviceReset): make the first call after a reset before any
+ *     stream capture too.
  *   - All calls on a device share the one array, which keeps the last call's
  *     contents; each call clears the parts that must start at zero (barrier
  *     counter, status word, row statistics) before its launch. Calls that

@@ -86,6 +86,18 @@ def test_argument_errors_without_launch(lib):
         a = list(dq)
         a[i] = v
         assert lib.ee_dequant_weight(*a) == rc, (i, v)
+    # ee_attention(q, ldq, k, ldk, v, ldv, out, ldo, batch, heads, hd, n_q, n_k, q_rows, k_rows, act, stream)
+    at = [16, 1024, 16, 2048, 16, 2048, 16, 1024, 1, 16, 64, 50, 256, 50, 256, _lib.EE_BF16, None]
+    for i, v, rc in ((0, 0, 1),                       # no q
+                     (10, 96, 9),                     # head size 96
+                     (11, 65, 9),                     # more than 64 queries
+                     (13, 49, 2),                     # fewer q rows per item than queries
+                     (13, 1 << 31, 2),                # q rows per item beyond 32 bits
+                     (14, 1 << 31, 2),                # k rows per item beyond 32 bits
+                     (1, 8, 2)):                      # row stride below the heads' width
+        a = list(at)
+        a[i] = v
+        assert lib.ee_attention(*a) == rc, (i, v)
     assert lib.ee_flow_sample(None, 0, 0, 0, 10, 0, 0, 0, None) == 1
     assert lib.ee_barrier_selftest(None, 1000, None) == 1
     assert lib.ee_barrier_selftest(16, 0, None) == 1
@@ -132,3 +144,35 @@ def test_cpu_tensors_fail_loudly():
     with pytest.raises(RuntimeError, match="no CPU path"):
         wq_linear(torch.zeros(2, 128), torch.zeros(8, 128, dtype=torch.int8), torch.ones(8, 1),
                   None, 128, 8)
+
+
+def test_quant_operand_shapes_checked_before_any_call():
+    """The C ABI sees raw pointers and cannot check that scales / zero points
+    are [N, K / group]; the Python entry points do, before the device is
+    touched (a mismatch would otherwise read past the scales on the GPU)."""
+    from embodied_efficiency_b200 import wq_linear
+    from embodied_efficiency_b200.wq_gemm import dequant_weight
+    x = torch.zeros(2, 256)
+    w8 = torch.zeros(8, 256, dtype=torch.int8)
+    w4 = torch.zeros(8, 128, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="scales have shape"):
+        wq_linear(x, w8, torch.ones(8, 1), None, 128, 8)          # group 128 needs [8, 2]
+    with pytest.raises(ValueError, match="scales have shape"):
+        wq_linear(x, w4, torch.ones(8, 4), None, 128, 4)
+    with pytest.raises(ValueError, match="does not divide"):
+        wq_linear(x, w8, torch.ones(8, 3), None, 96, 8)
+    with pytest.raises(ValueError, match="need scales"):
+        wq_linear(x, w8, None, None, 128, 8)
+    with pytest.raises(ValueError, match="float32 or float16"):
+        wq_linear(x, w8, torch.ones(8, 2, dtype=torch.float64), None, 128, 8)
+    with pytest.raises(ValueError, match="zeros have shape"):
+        wq_linear(x, w4, torch.ones(8, 2), None, 128, 4, zeros=torch.zeros(8, 1))
+    with pytest.raises(ValueError, match="int8 weights"):
+        wq_linear(x, w8.to(torch.uint8), torch.ones(8, 2), None, 128, 8)
+    with pytest.raises(ValueError, match="scales have shape"):
+        dequant_weight(w4, torch.ones(2, 8), 128, 4, torch.bfloat16)
+    with pytest.raises(ValueError, match="bits must be"):
+        wq_linear(x, w8, torch.ones(8, 2), None, 128, 3)
+    # well-formed operands get as far as the device check
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        wq_linear(x, w8, torch.ones(8, 2), None, 128, 8)

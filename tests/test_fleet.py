@@ -112,3 +112,27 @@ def test_fleet_gpu_matches_single_calls(cuda):
         one = flow_sample(m, x0.to(cuda).bfloat16(), 10, kv).float().cpu()
         err = (got[i:i + 1] - one).abs().max() / one.abs().max()
         assert err < 2e-2, (i, float(err))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,chunk", [(6, 4), (40, 40), (64, 32)])
+def test_fleet_graphs_match_direct_calls(cuda, n, chunk):
+    """Each chunk's call captured as a CUDA graph (fused launch for small
+    chunks, the layer-by-layer path from 1024 tokens on) replays what the
+    directly dispatched calls compute, fleet step after fleet step."""
+    from embodied_efficiency_b200 import ActionExpert, ActionExpertConfig, quantize_model_triton, synth
+    cfg = ActionExpertConfig(d_model=256, n_layers=2, n_heads=4, prefix_len=32)
+    params, _, _ = synth.workload(cfg, seed=4)
+    m = ActionExpert(cfg)
+    m.load_state_dict(params)
+    m = m.to(cuda).bfloat16().eval()
+    quantize_model_triton(m, bits=4)
+    req = lambda i: synth.fleet_request(cfg, i)  # noqa: E731
+    direct = FleetSampler(n, 0, 1, chunk=chunk, expert=m, device=cuda, graphs=False).stage(req).run().actions
+    fs = FleetSampler(n, 0, 1, chunk=chunk, expert=m, device=cuda).stage(req)
+    assert fs._graphs is not None and len(fs._graphs) == len(chunk_bounds(0, n, chunk))
+    for _ in range(2):
+        got = fs.run().actions
+        err = float((got - direct).abs().max() / direct.abs().max())
+        print(f"fleet n={n} chunk={chunk}: graph vs direct max rel diff {err:.3e}")
+        assert err < 2e-2

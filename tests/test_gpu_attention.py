@@ -1,7 +1,9 @@
-"""GPU parity of the attention launch (ee_attention) against
-F.scaled_dot_product_attention, the op it replaces on the layer-by-layer path
-(kernel/flow_expert.py:86, :91): self-attention read in place from a fused
-[q | k | v] projection and cross-attention to a [batch, P, 2d] prefix K/V."""
+"""GPU parity of the attention launch (ee_attention) against an fp32
+reference -- F.scaled_dot_product_attention on the same bf16 / fp16 inputs
+upcast to fp32 -- and against the bf16 / fp16 SDPA call it replaces on the
+layer-by-layer path (kernel/flow_expert.py:86, :91): self-attention read in
+place from a fused [q | k | v] projection and cross-attention to a
+[batch, P, 2d] prefix K/V."""
 import pytest
 import torch
 import torch.nn.functional as F
@@ -31,16 +33,23 @@ def test_matches_sdpa(cuda, dtype, b, n, h, hd, p):
     qkv = torch.randn(b, n, 3 * d, generator=g).to(cuda, dtype)
     a = _attention(qkv, 3 * d, qkv[..., d:], 3 * d, qkv[..., 2 * d:], 3 * d, b, h, hd, n, n, n, n)
     q, k, v = qkv.chunk(3, dim=-1)
-    ref = _merge(F.scaled_dot_product_attention(_split(q, h), _split(k, h), _split(v, h)))
-    torch.cuda.synchronize()
-    assert float((a.float() - ref.float()).abs().max()) <= TOL * float(ref.float().abs().max())
+    _check(a, _split(q, h), _split(k, h), _split(v, h))
     kv = torch.randn(b, p, 2 * d, generator=g).to(cuda, dtype)
     qc = torch.randn(b, n, d, generator=g).to(cuda, dtype)
     kk, vv = _split(kv[..., :d], h), _split(kv[..., d:], h)
     a = _attention(qc, d, kk, 2 * d, vv, 2 * d, b, h, hd, n, p, n, p)
-    ref = _merge(F.scaled_dot_product_attention(_split(qc, h), kk, vv))
+    _check(a, _split(qc, h), kk, vv)
+
+
+def _check(a, q, k, v):
+    """max |a - ref| / max |ref| <= TOL against the fp32 reference and against
+    the same-dtype SDPA."""
+    ref32 = _merge(F.scaled_dot_product_attention(q.float(), k.float(), v.float()))
+    ref = _merge(F.scaled_dot_product_attention(q, k, v)).float()
     torch.cuda.synchronize()
-    assert float((a.float() - ref.float()).abs().max()) <= TOL * float(ref.float().abs().max())
+    af = a.float()
+    assert float((af - ref32).abs().max()) <= TOL * float(ref32.abs().max())
+    assert float((af - ref).abs().max()) <= TOL * float(ref.abs().max())
 
 
 def test_rejects_long_query_blocks(cuda):

@@ -1,5 +1,7 @@
-"""GPU parity of the LayerNorm row kernel (ee_layer_norm) against torch's
-nn.LayerNorm, the op it replaces on the layer-by-layer path."""
+"""GPU parity of the LayerNorm row kernel (ee_layer_norm) against an fp32
+reference (F.layer_norm of the same inputs upcast to fp32) and against
+torch's bf16 / fp16 nn.LayerNorm, the op it replaces on the layer-by-layer
+path."""
 import pytest
 import torch
 import torch.nn.functional as F
@@ -26,8 +28,13 @@ def test_matches_torch_layer_norm(cuda, dtype, rows, cols):
     w = (torch.randn(cols, generator=g) * 0.5 + 1).to(cuda, dtype)
     b = (torch.randn(cols, generator=g) * 0.1).to(cuda, dtype)
     y, ref = _ln(x, w, b, 1e-5)
+    ref32 = F.layer_norm(x.float(), (cols,), w.float(), b.float(), 1e-5)
     torch.cuda.synchronize()
     ulp = 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10
+    # fp32 statistics, one rounding of the fp32 result: within half a unit
+    # in the last place of the fp32 reference (plus summation-order noise)
+    d32 = (y.float() - ref32).abs()
+    assert bool((d32 <= 0.5 * ulp * ref32.abs() * 1.01 + 1e-5).all())
     # fp32 statistics differ from torch's only in summation order: at most one
     # rounding step of the output apart, and almost everywhere identical
     diff = (y.float() - ref.detach().float()).abs()
