@@ -70,7 +70,22 @@ struct GemmArgs {
   // records EE_ERR_TIMEOUT, and its limit
   int* status;
   unsigned long long timeout_ns;
+  // built with EE_TRACE_DETAIL only: globaltimer stamps of this CTA's first
+  // unit at its serial steps (entry, staged, normalised, MMAs done, partials
+  // pushed, partials received, reduced, stored, statistics), or null
+  unsigned long long* dtr;
 };
+
+#ifdef EE_TRACE_DETAIL
+#define EE_STAMP(a, i)                                                  \
+  do {                                                                  \
+    if ((a).dtr && threadIdx.x == 0) (a).dtr[i] = globaltimer();        \
+  } while (0)
+#else
+#define EE_STAMP(a, i) \
+  do {                 \
+  } while (0)
+#endif
 
 // Shared memory of a GEMM unit (byte offsets from the dynamic base).
 //   x    activation slice [64 tok][KS] (16-byte chunks swizzled, see
@@ -531,6 +546,7 @@ struct Gemm {
     const int fit = (int)(sm.pre_bytes / pre_kb_bytes(KIND));
     const int npre = prw ? (KB < fit ? KB : fit) : 0;
 
+    EE_STAMP(a, 0);
     if (active) {
       // 1. activation slice, norm weight / bias slice, residual tile -> smem
       const int cpr = KS / 8;  // 16-byte chunks per token row
@@ -622,6 +638,7 @@ struct Gemm {
       }
     }
     __syncthreads();
+    EE_STAMP(a, 1);
 
     float acc[8][4];  // mma.sync form: token tile j, fragment c
     float acct[32];   // tcgen05 form: row 32*(warp%4)+lane, tokens 32*(warp/4)+i
@@ -674,11 +691,13 @@ struct Gemm {
         }
         if (!TC) __syncthreads();  // the tcgen05 form syncs before its first MMA
       }
+      EE_STAMP(a, 2);
 
       if (TC) {
         // 4. tcgen05 MMAs (activations written by this thread -> async proxy first)
         fence_proxy_async_smem();
         mma_tc(a, nt, kb0, KB, npre, NP, sx, smem, sm, acct);
+        EE_STAMP(a, 3);
       } else {
         // 4. mma.sync MMAs over this CTA's k-blocks (first pre_kb from the pre area)
         const bool smem_scales = KIND != EE_W_DENSE && L.scale_dtype == EE_F32 && KB <= kMaxKB;
@@ -752,6 +771,7 @@ struct Gemm {
 #pragma unroll
         for (int q = 0; q < 8; ++q)
           if (q < nq) st_async_f4(dst + 16 * q, acct[4 * q], acct[4 * q + 1], acct[4 * q + 2], acct[4 * q + 3], dbar);
+        EE_STAMP(a, 4);
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -776,6 +796,7 @@ struct Gemm {
         if (!mbar_wait(pbar, ppar, a.timeout_ns) && a.status) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
         if (threadIdx.x == 0)
           *reinterpret_cast<volatile uint32_t*>(smem + sm.tc + kTcPPar) ^= 1u << parity;
+        EE_STAMP(a, 5);
       }
     } else {
       cluster_sync();  // every partial of this round has arrived
@@ -802,6 +823,7 @@ struct Gemm {
         }
       }
       __syncthreads();
+      EE_STAMP(a, 6);
 
       // 7. epilogue on 8-column chunks: bias, round, GELU / residual, one
       //    16-byte store per chunk (scalar stores for a ragged end)
@@ -838,6 +860,7 @@ struct Gemm {
             if (n0 + e < L.n) dst[e] = Act<T>::from_f(v[e]);
         }
       }
+      EE_STAMP(a, 7);
       // 8. row statistics of this CTA's columns (column order), one slot each
       if (a.out_stats) {
         __syncthreads();
@@ -859,6 +882,7 @@ struct Gemm {
       }
     }
     __syncthreads();  // shared memory reuse by the next unit
+    EE_STAMP(a, 8);
   }
 
   // All units of a GEMM in rounds over the cluster slots; `pre` applies to
@@ -871,11 +895,14 @@ struct Gemm {
     const int slots = (int)cl_count() * per_cluster;
     const int slot = (int)cl_id() * per_cluster + ((int)cl_rank() >> a.lsplit);
     const int rounds = (units + slots - 1) / slots;
+    GemmArgs ar = a;
+    EE_STAMP(a, 12);
     for (int rd = 0; rd < rounds; ++rd) {
       const int u = rd * slots + slot;
       const bool act = u < units;
-      unit(a, act, act ? u % n_tiles : 0, act ? (u / n_tiles) * kMTile : 0, rd & 1, smem, sm,
+      unit(ar, act, act ? u % n_tiles : 0, act ? (u / n_tiles) * kMTile : 0, rd & 1, smem, sm,
            (rd == 0 && act) ? pre : nullptr);
+      ar.dtr = nullptr;  // stamps describe the first round only
     }
   }
   // Start the prefetch of this CTA's first unit; returns whether it has one.

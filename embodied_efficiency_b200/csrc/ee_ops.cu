@@ -105,7 +105,10 @@ template <typename T> int launch_tc(const GemmArgs& g, int* status, cudaStream_t
 
 // Token count up to which the warp-MMA streaming kernel is used; above it
 // the tcgen05 kernel.
-constexpr int kStreamMaxM = 32;
+#ifndef EE_STREAM_MAX_M
+#define EE_STREAM_MAX_M 32
+#endif
+constexpr int kStreamMaxM = EE_STREAM_MAX_M;
 
 // Status word of the GEMM kernels (first error since the last reset).
 static __device__ int g_gemm_status;

@@ -36,6 +36,15 @@ namespace ee {
 
 enum { PH_EMB = 0, PH_TPROJ, PH_HEAD, PH_GEMM, PH_ATTN_SELF, PH_ATTN_CROSS, PH_TAILHEAD, PH_TAIL };
 
+// globaltimer stamps per (phase, CTA) in the optional trace: work done and
+// barrier left; a build with EE_TRACE_DETAIL adds the GEMM units' step stamps
+// (slots 2..10)
+#ifdef EE_TRACE_DETAIL
+constexpr int kTraceSlots = 16;
+#else
+constexpr int kTraceSlots = 2;
+#endif
+
 struct Ctx {
   ee_expert ex;
   const void* x_in;
@@ -536,6 +545,9 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
 
   for (int p = 0; p < P; ++p) {
     const Phase ph = decode(c, p);
+#ifdef EE_TRACE_DETAIL
+    if (c.trace && threadIdx.x == 0) c.trace[((size_t)p * gridDim.x + blockIdx.x) * kTraceSlots + 12] = globaltimer();
+#endif
     switch (ph.type) {
       case PH_EMB: {
         const int half = d / 2;
@@ -555,9 +567,15 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
         break;
       }
       case PH_TPROJ:
-      case PH_GEMM:
-        gemm_dispatch<T>(make_gemm(c, ph, smem), smem, c.sm, have_pre ? &pre : nullptr, false, nullptr);
+      case PH_GEMM: {
+        GemmArgs ga = make_gemm(c, ph, smem);
+#ifdef EE_TRACE_DETAIL
+        if (c.trace) ga.dtr = c.trace + ((size_t)p * gridDim.x + blockIdx.x) * kTraceSlots + 2;
+        if (c.trace && threadIdx.x == 0) c.trace[((size_t)p * gridDim.x + blockIdx.x) * kTraceSlots + 13] = globaltimer();
+#endif
+        gemm_dispatch<T>(ga, smem, c.sm, have_pre ? &pre : nullptr, false, nullptr);
         break;
+      }
       case PH_ATTN_SELF:
       case PH_ATTN_CROSS: {
         AttnArgs at{};
@@ -606,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
     have_pre = false;
     __syncthreads();  // this CTA is done with phase p (and its shared memory)
     if (c.trace && threadIdx.x == 0)
-      c.trace[((size_t)p * gridDim.x + blockIdx.x) * 2] = globaltimer();
+      c.trace[((size_t)p * gridDim.x + blockIdx.x) * kTraceSlots] = globaltimer();
     if (p + 1 < P) {
       // arrive first, then start the next GEMM phase's weight copies while
       // the other CTAs finish (the copies read only constant weights)
@@ -615,6 +633,9 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
       const Phase nx = decode(c, p + 1);
       if (nx.type == PH_GEMM || nx.type == PH_TPROJ)
         have_pre = gemm_dispatch<T>(make_gemm(c, nx, smem), smem, c.sm, nullptr, true, &pre);
+#ifdef EE_TRACE_DETAIL
+      if (c.trace && threadIdx.x == 0) c.trace[((size_t)p * gridDim.x + blockIdx.x) * kTraceSlots + 11] = globaltimer();
+#endif
       if (!grid_wait(c, target)) {
         cp_async_wait<0>();
         release_tmem();
@@ -622,7 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1) sampler_kernel(const __grid_const
       }
     }
     if (c.trace && threadIdx.x == 0)
-      c.trace[((size_t)p * gridDim.x + blockIdx.x) * 2 + 1] = globaltimer();
+      c.trace[((size_t)p * gridDim.x + blockIdx.x) * kTraceSlots + 1] = globaltimer();
   }
   release_tmem();
 }

@@ -46,6 +46,10 @@ constexpr int kStreamCThreads = kStreamCWarps * 32;
 constexpr int kStreamWarps = kStreamCWarps + 1;  // + 1 producer warp
 constexpr int kStreamThreads = kStreamWarps * 32;
 constexpr int kStreamMaxTokens = 64;
+#ifndef EE_STREAM_MAX_STAGES
+#define EE_STREAM_MAX_STAGES 24
+#endif
+constexpr int kStreamMaxStages = EE_STREAM_MAX_STAGES;  // ring depth cap
 
 struct StreamArgs {
   ee_linear w;
@@ -111,24 +115,24 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
     mbar_fence_init();
   }
-  // consumers: start the scale / zero-point loads of every k-block now (up
-  // to 4 in flight per thread); they land in shared memory below
+  // consumers: the scale / zero point of (row r, k-block kb) is entry
+  // kb * 128 + r; the first 4 per thread are requested now (in flight while
+  // the producer starts its copies), the rest after the CTA barrier below
   float sv[4], zv[4];
-  if (KIND != EE_W_DENSE && warp < kStreamCWarps) {
-    const int ng = L.k / L.group;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = threadIdx.x + kStreamCThreads * u;
-      sv[u] = zv[u] = 0.f;
-      if (i < a.kbc * 128) {
-        const int kb = i >> 7, r = i & 127;
-        const int n = min(n0 + r, L.n - 1);
-        const size_t si = (size_t)n * ng + ((size_t)(kb_first + kb) * kKBlock) / L.group;
-        sv[u] = L.scale_dtype == EE_F32 ? __ldg(reinterpret_cast<const float*>(L.scales) + si)
-                                        : __half2float(__ldg(reinterpret_cast<const __half*>(L.scales) + si));
-        if (KIND == EE_W_UINT4Z) zv[u] = __half2float(__ldg(reinterpret_cast<const __half*>(L.zeros) + si));
-      }
+  auto load_scale = [&](int i, float& sc, float& zp) {
+    sc = zp = 0.f;
+    if (i < a.kbc * 128) {
+      const int kb = i >> 7, r = i & 127;
+      const int n = min(n0 + r, L.n - 1);
+      const size_t si = (size_t)n * (L.k / L.group) + ((size_t)(kb_first + kb) * kKBlock) / L.group;
+      sc = L.scale_dtype == EE_F32 ? __ldg(reinterpret_cast<const float*>(L.scales) + si)
+                                   : __half2float(__ldg(reinterpret_cast<const __half*>(L.scales) + si));
+      if (KIND == EE_W_UINT4Z) zp = __half2float(__ldg(reinterpret_cast<const __half*>(L.zeros) + si));
     }
+  };
+  if (KIND != EE_W_DENSE && warp < kStreamCWarps) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) load_scale(threadIdx.x + kStreamCThreads * u, sv[u], zv[u]);
   }
 
   __syncthreads();
@@ -177,12 +181,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     float* sbias = reinterpret_cast<float*>(smem + a.off_bias);  // [RS]
     const int nbase = n0 + rank * RS;
     if (KIND != EE_W_DENSE) {
+      for (int base = 0; base < a.kbc * 128; base += 4 * kStreamCThreads) {
+        if (base > 0) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = threadIdx.x + kStreamCThreads * u;
-        if (i < a.kbc * 128) {
-          scal[i] = sv[u];
-          if (KIND == EE_W_UINT4Z) zero[i] = zv[u];
+          for (int u = 0; u < 4; ++u) load_scale(base + threadIdx.x + kStreamCThreads * u, sv[u], zv[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int i = base + threadIdx.x + kStreamCThreads * u;
+          if (i < a.kbc * 128) {
+            scal[i] = sv[u];
+            if (KIND == EE_W_UINT4Z) zero[i] = zv[u];
+          }
         }
       }
     }
@@ -399,7 +409,6 @@ int stream_launch_k(const GemmArgs& g, int* status, cudaStream_t st, bool* used)
   while (S > 1 && ((K % (kKBlock * S)) != 0 || U * S > dp->sms)) S >>= 1;
   const int lsplit = S == 8 ? 3 : (S == 4 ? 2 : (S == 2 ? 1 : 0));
   const int kbc = K / (kKBlock * S), RS = 128 / S;
-  if (kbc > 16) return EE_OK;  // scales are staged 4 per consumer thread
   // few tokens: the activation slice stays resident (<= 64 KB)
   const uint32_t xres_bytes = (uint32_t)kbc * 2048u * JT;
   const int xres = (JT <= 4 && xres_bytes <= 65536u) ? 1 : 0;
@@ -408,11 +417,13 @@ int stream_launch_k(const GemmArgs& g, int* status, cudaStream_t st, bool* used)
   const uint32_t scal = KIND == EE_W_DENSE ? 0u : (uint32_t)kbc * 128u * 4u * (KIND == EE_W_UINT4Z ? 2u : 1u);
   const uint32_t recv = 256u * ps * 4u;
   const uint32_t res = g.epi == EPI_RESID ? (uint32_t)(8 * JT * RS * 2) : 0u;
-  const uint32_t fixed = 16u * 8u + 16u + scal + 16u + recv + 16u + res + 16u + (uint32_t)RS * 4u + 1024u +
+  const uint32_t fixed = 16u * (uint32_t)kStreamMaxStages + 16u + scal + 16u + recv + 16u + res + 16u + (uint32_t)RS * 4u + 1024u +
                          (xres ? xres_bytes + 1024u : 0u);
   if ((uint32_t)dp->smem_optin <= fixed + stage) return EE_OK;
+  // as many k-blocks in flight as shared memory holds (up to kStreamMaxStages):
+  // with one CTA per SM the ring depth is what keeps HBM busy
   int nst = (int)(((uint32_t)dp->smem_optin - fixed) / stage);
-  nst = nst < 8 ? nst : 8;
+  nst = nst < kStreamMaxStages ? nst : kStreamMaxStages;
   nst = nst < kbc ? nst : kbc;
   if (nst < 1) return EE_OK;
 

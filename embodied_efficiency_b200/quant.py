@@ -21,7 +21,12 @@ def quantize_weight(w: torch.Tensor, bits: int, group_size: int = 128):
     gs = group_size if inf % group_size == 0 else inf
     wg = w.float().reshape(out, inf // gs, gs)
     qmax = 2 ** (bits - 1) - 1
-    scale = (wg.abs().amax(dim=-1, keepdim=True) / qmax).clamp_min(1e-8)
+    amax = wg.abs().amax(dim=-1, keepdim=True)
+    # a tensor divisor, not the Python number: on CUDA, torch divides by a
+    # scalar as a multiplication by its reciprocal, which differs from the
+    # true quotient (what the reference computes on the CPU) in the last bit
+    # of some scales; tensor / tensor is a true division on either device
+    scale = (amax / torch.full_like(amax, qmax)).clamp_min(1e-8)
     q = torch.clamp(torch.round(wg / scale), -qmax - 1, qmax)
     return q.to(torch.int8), scale, gs
 
@@ -47,7 +52,8 @@ def quantize_weight_asym4(w: torch.Tensor, group_size: int = 128):
     wg = w.float().reshape(out, inf // gs, gs)
     wmin = wg.amin(dim=-1, keepdim=True)
     wmax = wg.amax(dim=-1, keepdim=True)
-    scale = ((wmax - wmin) / 15.0).clamp_min(2.0 ** -14).half().float()
+    rng = wmax - wmin
+    scale = (rng / torch.full_like(rng, 15.0)).clamp_min(2.0 ** -14).half().float()  # true division (see above)
     zero = torch.clamp(torch.round(-wmin / scale), 0, 15)
     q = torch.clamp(torch.round(wg / scale) + zero, 0, 15).to(torch.uint8)
     return (q.reshape(out, inf), scale.reshape(out, -1).half(), zero.reshape(out, -1).half(), gs)

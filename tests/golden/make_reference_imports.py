@@ -3,7 +3,7 @@
 drop-in layer aliases (flow_expert, triton_gemm, cudagraph, quant), as
 [file, module, name] triples. The reference is read as text only.
 
-    python tests/golden/make_reference_imports.py /root/reference
+    python tests/golden/make_reference_imports.py <reference checkout>
 """
 import ast
 import json
@@ -30,4 +30,6 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_reference_imports.py <path of the reference checkout>")
+    main(sys.argv[1])

@@ -130,6 +130,23 @@ def test_config2_sweep(cuda, k, kind, group):
         assert rel_err(y, ref) <= TOL, (m, k, kind, group, rel_err(y, ref))
 
 
+@pytest.mark.parametrize("n,k", [(8192, 8192), (6144, 2048), (8192, 2048), (2048, 8192), (1024, 16384)])
+@pytest.mark.parametrize("kind,group", [("int4", 128), ("int8", 128), ("int8", "pc"), ("int4z", 128), ("bf16", 0)])
+def test_large_weights_few_tokens(cuda, n, k, kind, group):
+    """Weights larger than a streaming CTA's old 16-k-block limit (K / split
+    up to 64 k-blocks per CTA, deep stage rings) at the batch-1 token counts,
+    against the oracle; the Pi0-scale expert's GEMM shapes among them."""
+    rng = np.random.default_rng(n + k)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    grp = k if group == "pc" else group
+    for m in (1, 7, 16, 32, 50, 64):
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        y, ref = _run(cuda, x, w, kind, grp)
+        assert rel_err(y, ref) <= TOL, (m, n, k, kind, group, rel_err(y, ref))
+    from embodied_efficiency_b200 import wq_gemm
+    assert wq_gemm.gemm_status() == 0
+
+
 @pytest.mark.parametrize("m,n,k", [(3, 200, 128), (77, 130, 384), (65, 1000, 640), (1, 8, 256),
                                    (129, 4096, 1024), (700, 96, 2048)])
 @pytest.mark.parametrize("kind", ["int8", "int4", "int4z", "bf16"])
