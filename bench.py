@@ -84,7 +84,9 @@ def step_bytes(cfg, bits, batch=1):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while running.
+    Entering waits (up to 5 s) for the first sample, so a short timed region
+    that starts afterwards is covered by samples."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -93,33 +95,48 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.lines = []
 
     def __enter__(self):
+        import threading
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return self
+        first = threading.Event()
+
+        def reader():
+            for ln in self.proc.stdout:
+                if ln.strip():
+                    self.lines.append(ln.strip())
+                    first.set()
+            first.set()
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        first.wait(5.0)
+        self.t_start = len(self.lines)  # samples taken before the timed region are not counted
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
-            time.sleep(0.25)
+            time.sleep(0.1)
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-                out = ""
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            self.thread.join(timeout=5)
+            self.lines = self.lines[max(0, getattr(self, "t_start", 0) - 1):]
 
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
