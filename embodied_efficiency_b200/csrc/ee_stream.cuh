@@ -15,14 +15,14 @@
 //    stage guarded by a "full" mbarrier (TMA transaction bytes) and an
 //    "empty" mbarrier (the consuming warps), so up to nst k-blocks are in
 //    flight per SM;
-//  * sixteen consumer warps: warp = (row group rw: 16 rows, k group kg), the
-//    two k groups taking alternate k-blocks (four warps per scheduler, so
-//    one warp's dependency stalls are covered by the others). Each warp
+//  * 8 x kStreamKG consumer warps: warp = (row group rw: 16 rows, k group
+//    kg), the k groups taking every kStreamKG-th k-block (several warps per
+//    scheduler, so one warp's dependency stalls are covered by the others). Each warp
 //    dequantises its 16 rows in registers (nibble / byte -> exact bf16/f16 integers, see
 //    ee_gemm.cuh) and runs m16n8k16 MMAs with the weights as the A operand
 //    and the tokens as B; the fp32 per-(row, group) scale multiplies each
 //    k-block's partial sum;
-//  * the 2*S partial tiles of a unit (S CTAs x 2 k groups) are pushed over
+//  * the kStreamKG*S partial tiles of a unit (S CTAs x kStreamKG k groups) are pushed over
 //    distributed shared memory to the CTA that owns their rows (128/S rows
 //    per CTA), summed there in a fixed order (deterministic), and the owner
 //    applies bias / GELU / residual and stores 16-byte chunks.
@@ -41,7 +41,11 @@
 
 namespace ee {
 
-constexpr int kStreamCWarps = 16;  // consumer warps: 8 row groups x 2 k groups
+#ifndef EE_STREAM_KG
+#define EE_STREAM_KG 2
+#endif
+constexpr int kStreamKG = EE_STREAM_KG;            // k groups: consumer warp sets taking every kStreamKG-th k-block
+constexpr int kStreamCWarps = 8 * kStreamKG;       // consumer warps: 8 row groups x kStreamKG k groups
 constexpr int kStreamCThreads = kStreamCWarps * 32;
 constexpr int kStreamWarps = kStreamCWarps + 1;  // + 1 producer warp
 constexpr int kStreamThreads = kStreamWarps * 32;
@@ -111,7 +115,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     if (!a.xres) tma_prefetch_map(&tx);
     for (int s = 0; s < a.nst; ++s) {
       mbar_init(bar_full + 8u * s, 1);
-      mbar_init(bar_empty + 8u * s, kStreamCWarps / 2);
+      mbar_init(bar_empty + 8u * s, 8);  // the 8 row-group warps of the k group that consumes the stage
     }
     mbar_fence_init();
   }
@@ -236,7 +240,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       for (int c = 0; c < 4; ++c) acc[0][j][c] = 0.f;
 
     int s = kg % a.nst, sph = (kg / a.nst) & 1;  // ring position of k-block kb (advanced below)
-    for (int kb = kg; kb < a.kbc; kb += 2) {
+    for (int kb = kg; kb < a.kbc; kb += kStreamKG) {
       if (!mbar_wait(bar_full + 8u * s, (uint32_t)sph, a.timeout_ns)) {
         if (lane == 0) atomicCAS(a.status, 0, (int)EE_ERR_TIMEOUT);
         break;
@@ -301,7 +305,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_empty + 8u * s);
-      s += 2;
+      s += kStreamKG;
       while (s >= a.nst) {
         s -= a.nst;
         sph ^= 1;
@@ -310,7 +314,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 
     // push this warp's partial tile: rows of rank o go to rank o's receive area
     const uint32_t recv = sb + a.off_recv;
-    const int qslot = rank * 2 + kg;
+    const int qslot = rank * kStreamKG + kg;
     const int rshift = 7 - a.lsplit;
 #pragma unroll
     for (int mi = 0; mi < 1; ++mi)
@@ -329,11 +333,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   cluster_sync();  // every partial of the unit has arrived; the ring is idle
 
   if (warp < kStreamCWarps) {
-    // sum the 2*S partials of this CTA's RS rows in slot order
+    // sum the kStreamKG*S partials of this CTA's RS rows in slot order
     const int ntok = min(JT, (a.M + 7) >> 3) * 8;
     const float* R = reinterpret_cast<const float*>(smem + a.off_recv);
     float* E = reinterpret_cast<float*>(smem);  // [ntok][RS], reuses the ring
-    const int nq = 2 * S;
+    const int nq = kStreamKG * S;
     for (int i = threadIdx.x; i < RS * (ntok >> 2); i += kStreamCThreads) {
       const int row = i % RS, c4 = i / RS;
       float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -415,7 +419,7 @@ int stream_launch_k(const GemmArgs& g, int* status, cudaStream_t st, bool* used)
   const uint32_t stage = align_up(stream_wbytes<KIND>() + (xres ? 0u : 2048u * JT), 1024u);
   const int ps = 8 * JT + 4;
   const uint32_t scal = KIND == EE_W_DENSE ? 0u : (uint32_t)kbc * 128u * 4u * (KIND == EE_W_UINT4Z ? 2u : 1u);
-  const uint32_t recv = 256u * ps * 4u;
+  const uint32_t recv = (uint32_t)kStreamKG * 128u * ps * 4u;
   const uint32_t res = g.epi == EPI_RESID ? (uint32_t)(8 * JT * RS * 2) : 0u;
   const uint32_t fixed = 16u * (uint32_t)kStreamMaxStages + 16u + scal + 16u + recv + 16u + res + 16u + (uint32_t)RS * 4u + 1024u +
                          (xres ? xres_bytes + 1024u : 0u);
@@ -425,6 +429,10 @@ int stream_launch_k(const GemmArgs& g, int* status, cudaStream_t st, bool* used)
   int nst = (int)(((uint32_t)dp->smem_optin - fixed) / stage);
   nst = nst < kStreamMaxStages ? nst : kStreamMaxStages;
   nst = nst < kbc ? nst : kbc;
+  // a stage that is reused must always be consumed by the same k group
+  // (k-block kb lands in stage kb % nst and is consumed by group kb % kStreamKG):
+  // a waiter of another group could otherwise be two barrier phases ahead
+  if (nst < kbc) nst -= nst % kStreamKG;
   if (nst < 1) return EE_OK;
 
   StreamArgs a{};
