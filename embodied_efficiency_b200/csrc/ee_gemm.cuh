@@ -598,6 +598,12 @@ struct Gemm {
             sx += v[i].x;
             sxx += v[i].y;
           }
+          // more than 128 slots (d_model 2048 with 8-column slots): the rest, in order
+          for (int q = part + 128; q < a.stat_slots; q += 4) {
+            const float2 w = ld_act_f2(sp + 2 * q);
+            sx += w.x;
+            sxx += w.y;
+          }
         }
         sx += __shfl_xor_sync(0xffffffffu, sx, 1);
         sxx += __shfl_xor_sync(0xffffffffu, sxx, 1);

@@ -692,10 +692,15 @@ inline int sampler_cluster(const ee_expert& ex) {
 }
 
 // largest K slice a unit stages: what the widest GEMM (K = max(d, hidden))
-// needs with the whole cluster splitting it, at least 512
+// needs with the whole cluster splitting it, at least 512. Where an 8-CTA
+// cluster would leave a wider slice (an MLP of 8192 at d_model 2048) and the
+// width splits into 16 k-block slices, the plan is for 16-CTA clusters
+// (non-portable; the launch geometry then rejects 8-CTA plans, whose split
+// would exceed this cap), keeping the staged slice at 512.
 inline int sampler_ks_cap(const ee_expert& ex) {
   const int kmax = ex.hidden > ex.d_model ? ex.hidden : ex.d_model;
-  const int need = kmax / sampler_cluster(ex);
+  int need = kmax / sampler_cluster(ex);
+  if (need > 512 && sampler_cluster(ex) == 8 && (ex.d_model / 128) % 16 == 0) need = kmax / 16;
   return need > 512 ? need : 512;
 }
 

@@ -228,7 +228,7 @@ class ActionExpert(nn.Module):
         """kernel/flow_expert.py:117-124: velocity for x_act [B,H,A] at times t [B]."""
         _lib.require_cuda(x_act)
         b = x_act.shape[0]
-        if _fused.supports(self, b):
+        if _fused.preferred(self, b, FUSED_MAX_TOKENS):
             v = self.plan(b, prefix_kv).run(x_act, 1, t0=t, mode=_lib.EE_MODE_VELOCITY)
             return v.to(x_act.dtype)
         return self.forward_layers(x_act, t, prefix_kv)
@@ -298,7 +298,7 @@ def flow_sample(expert, x_init: torch.Tensor, n_steps: int, prefix_kv, path: str
     fused_ok = _fused.supports(expert, b)
     if path == "fused" and not fused_ok:
         raise ValueError("the fused launch does not cover this expert / batch")
-    use_fused = fused_ok and (path == "fused" or (path == "auto" and b * expert.cfg.horizon <= FUSED_MAX_TOKENS))
+    use_fused = fused_ok and (path == "fused" or (path == "auto" and _fused.preferred(expert, b, FUSED_MAX_TOKENS)))
     if use_fused:
         return get_plan(expert, b, prefix_kv).run(x_init, n_steps).to(x_init.dtype)
     x = x_init

@@ -34,7 +34,7 @@ class GraphedSampler:
         b = x_template.shape[0]
         # the same choice flow_sample makes: the single fused launch up to
         # FUSED_MAX_TOKENS tokens, else the layer-by-layer path (captured too)
-        self.fused = _fused.supports(expert, b) and b * expert.cfg.horizon <= _expert.FUSED_MAX_TOKENS
+        self.fused = _fused.preferred(expert, b, _expert.FUSED_MAX_TOKENS)
         self.plan = get_plan(expert, b, self.prefix_kv) if self.fused else None
         if self.fused:
             self.static_out = torch.empty_like(self.static_in, dtype=self.plan.act)

@@ -199,11 +199,15 @@ def _c5_params():
     return _C5_CACHE["p16"]
 
 
-@pytest.mark.parametrize("bits,batch,steps", [(4, 1, 10), (4, 8, 2), (8, 1, 10), (8, 8, 2)])
-def test_config5_scale_against_oracle(cuda, bits, batch, steps):
+@pytest.mark.parametrize("bits,batch,steps,path", [(4, 1, 10, "auto"), (4, 8, 2, "auto"), (4, 1, 2, "fused"),
+                                                  (8, 1, 10, "auto"), (8, 8, 2, "auto")])
+def test_config5_scale_against_oracle(cuda, bits, batch, steps, path):
     """Pi0-scale expert (d 2048, 18 blocks, 16 x 128 heads, MLP 8192, prefix
     816; 1.21 B parameters), int4 / int8 group-128, batch 1 and 8 with each
-    request's own noise and prefix: action error against the oracle."""
+    request's own noise and prefix: action error against the oracle. "auto"
+    runs layer by layer (faster at this size); "fused" is the single launch
+    with 16-CTA clusters (each CTA stages a 512-wide slice of the 8192-wide
+    MLP)."""
     from embodied_efficiency_b200 import ActionExpert, ActionExpertConfig, flow_sample, quantize_model_triton, synth
     cfg = ActionExpertConfig(**_C5)
     p16 = _c5_params()
@@ -212,7 +216,7 @@ def test_config5_scale_against_oracle(cuda, bits, batch, steps):
     m.load_state_dict(p16)
     m = m.to(cuda).bfloat16().eval()
     quantize_model_triton(m, bits=bits)
-    y = flow_sample(m, x0.to(cuda).bfloat16(), steps, m.encode(prefix.to(cuda))).float().cpu()
+    y = flow_sample(m, x0.to(cuda).bfloat16(), steps, m.encode(prefix.to(cuda)), path=path).float().cpu()
     del m
     torch.cuda.empty_cache()
     ocfg = OS.Cfg(**_C5)
