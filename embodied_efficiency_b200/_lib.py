@@ -76,6 +76,10 @@ SIGNATURES = {
                                 c_float, c_int32, c_void_p]),
     "ee_attention": (c_int32, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
                                c_int32, c_int32, c_int32, c_int32, c_int32, c_int64, c_int64, c_int32, c_void_p]),
+    "ee_time_embed": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
+    "ee_expert_head": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32,
+                                 c_int64, c_int64, c_int32, c_void_p]),
+    "ee_euler_step": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_float, c_int32, c_void_p]),
     "ee_flow_sample_traced": (c_int32, [ctypes.POINTER(Expert), c_void_p, c_void_p, c_void_p, c_int32,
                                         c_int32, c_void_p, c_size_t, c_void_p, c_void_p]),
     "ee_flow_sample_phases": (c_int32, [ctypes.POINTER(Expert), c_int32]),

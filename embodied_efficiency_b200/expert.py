@@ -113,6 +113,63 @@ def _attention(q, ldq, k, ldk, v, ldv, b: int, h: int, hd: int, n_q: int, n_k: i
     return out
 
 
+_FREQS: dict = {}
+
+
+def _row_kernels_ok(x: torch.Tensor) -> bool:
+    return x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and x.is_contiguous() and x.data_ptr() % 16 == 0
+
+
+def _time_embedding_act(t: torch.Tensor, d: int, dtype) -> torch.Tensor:
+    """timestep_embedding(t, d).to(dtype) (kernel/flow_expert.py:38-48, :120) on
+    the row kernel ``ee_time_embed`` (the fused launch's frequencies and
+    arithmetic) for CUDA bf16 / fp16; other inputs take the torch helper."""
+    if not (t.is_cuda and dtype in (torch.bfloat16, torch.float16) and t.dtype == dtype and d % 2 == 0):
+        return timestep_embedding(t, d).to(dtype)
+    key = (t.device, d)
+    freqs = _FREQS.get(key)
+    if freqs is None:
+        freqs = _FREQS[key] = _fused.time_freqs(d, t.device)
+    tc = t.contiguous()
+    emb = torch.empty(t.shape[0], d, device=t.device, dtype=dtype)
+    _lib.check(_lib.load().ee_time_embed(tc.data_ptr(), freqs.data_ptr(), emb.data_ptr(), t.shape[0], d,
+                                         _lib.act_code(dtype), _lib.stream_ptr(t.device)), "ee_time_embed")
+    return emb
+
+
+def _expert_head(expert, x_act: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+    """x = in_proj(x_act) + t_proj(temb(t))[:, None] (kernel/flow_expert.py:119-121):
+    t_proj on the dequant-GEMM, then ``ee_expert_head`` for the K = action_dim
+    in_proj, its bias and the broadcast add in one pass (bf16 / fp16 CUDA);
+    other inputs run the torch ops."""
+    cfg = expert.cfg
+    d, a = cfg.d_model, x_act.shape[-1]
+    ip = expert.in_proj
+    temb = _apply_linear(expert.t_proj, _time_embedding_act(t, d, x_act.dtype))
+    if not (_row_kernels_ok(x_act) and isinstance(ip, nn.Linear) and ip.weight.dtype == x_act.dtype
+            and (ip.bias is None or ip.bias.dtype == x_act.dtype) and a % 8 == 0 and a <= 64
+            and ip.weight.is_contiguous() and ip.weight.data_ptr() % 16 == 0 and temb.is_contiguous()):
+        return _apply_linear(ip, x_act) + temb[:, None, :]
+    b, h = x_act.shape[0], x_act.shape[1]
+    x = torch.empty(b, h, d, device=x_act.device, dtype=x_act.dtype)
+    _lib.check(_lib.load().ee_expert_head(x_act.data_ptr(), ip.weight.data_ptr(), _lib.ptr(ip.bias), temb.data_ptr(),
+                                          x.data_ptr(), b * h, a, d, h, d, _lib.act_code(x_act.dtype),
+                                          _lib.stream_ptr(x_act.device)), "ee_expert_head")
+    return x
+
+
+def _euler_step(x: torch.Tensor, v: torch.Tensor, t: torch.Tensor, dt: float):
+    """x = x + v * dt; t = t + dt (kernel/flow_expert.py:133-136) in place with
+    ``ee_euler_step`` (bf16 / fp16 CUDA), else as the torch ops; returns (x, t)."""
+    if (_row_kernels_ok(x) and _row_kernels_ok(t) and v.dtype == x.dtype and v.is_contiguous()
+            and v.shape == x.shape and t.dtype == x.dtype):
+        _lib.check(_lib.load().ee_euler_step(x.data_ptr(), v.data_ptr(), t.data_ptr(), x.numel(), t.shape[0],
+                                             float(dt), _lib.act_code(x.dtype), _lib.stream_ptr(x.device)),
+                   "ee_euler_step")
+        return x, t
+    return x + v * dt, t + dt
+
+
 def _apply_linear(mod, x, gelu: bool = False, residual=None):
     """A linear of the eager path on the sm_100a GEMM (cuBLAS only for K % 128 != 0),
     with GELU or ``residual +`` fused into the GEMM epilogue (the same roundings
@@ -237,9 +294,7 @@ class ActionExpert(nn.Module):
         """The same velocity computed layer by layer (sm_100a GEMMs with fused
         GELU / residual epilogues, the LayerNorm row kernel and the attention
         launch between them)."""
-        x = _apply_linear(self.in_proj, x_act)
-        temb = _apply_linear(self.t_proj, timestep_embedding(t, self.cfg.d_model).to(x.dtype))
-        x = x + temb[:, None, :]
+        x = _expert_head(self, x_act, t)
         for blk, kv in zip(self.blocks, prefix_kv):
             x = blk(x, kv)
         return _apply_linear(self.out_proj, _apply_norm(self.out_norm, x))
@@ -301,13 +356,12 @@ def flow_sample(expert, x_init: torch.Tensor, n_steps: int, prefix_kv, path: str
     use_fused = fused_ok and (path == "fused" or (path == "auto" and _fused.preferred(expert, b, FUSED_MAX_TOKENS)))
     if use_fused:
         return get_plan(expert, b, prefix_kv).run(x_init, n_steps).to(x_init.dtype)
-    x = x_init
+    x = x_init.contiguous().clone()  # updated in place below
     dt = 1.0 / n_steps
     t = torch.zeros(x.shape[0], device=x.device, dtype=x.dtype)
     for _ in range(n_steps):
         v = expert.forward_layers(x, t, prefix_kv) if hasattr(expert, "forward_layers") else expert(x, t, prefix_kv)
-        x = x + v * dt
-        t = t + dt
+        x, t = _euler_step(x, v, t, dt)
     return x
 
 

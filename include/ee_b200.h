@@ -18,6 +18,9 @@
  *                         GEMM's rounding (kernel/triton_gemm.py:91-94, :127-134)
  *   ee_layer_norm         kernel/flow_expert.py:51-95 the blocks' nn.LayerNorm
  *   ee_attention          kernel/flow_expert.py:86, :91 scaled_dot_product_attention
+ *   ee_time_embed         kernel/flow_expert.py:38-48 timestep_embedding (+ the .to(dtype) of :120)
+ *   ee_expert_head        kernel/flow_expert.py:119-121 in_proj(x) + t_proj(temb)[:, None]
+ *   ee_euler_step         kernel/flow_expert.py:133-136 x = x + v * dt; t = t + dt
  *   ee_flow_sample        kernel/flow_expert.py:127-137 flow_sample, run as
  *                         one fused launch over kernel/flow_expert.py:117-124
  *                         ActionExpert.forward and :83-95 Block.forward
@@ -147,6 +150,24 @@ int ee_layer_norm(const void* x, const void* weight, const void* bias, void* y, 
 int ee_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* out,
                  int64_t ldo, int32_t batch, int32_t n_heads, int32_t head_dim, int32_t n_q, int32_t n_k,
                  int64_t q_rows_per_b, int64_t k_rows_per_b, int32_t act_dtype, ee_stream_t stream);
+
+/* Row operations of the layer-by-layer sampler path (act dtype throughout).
+ * ee_time_embed: emb[b] = [cos(t_b * f * 1000), sin(t_b * f * 1000)] for the
+ * dim / 2 fp32 frequencies f (kernel/flow_expert.py:41-43), one rounding to the
+ * act dtype; emb is [batch][dim].
+ * ee_expert_head: x[m] = round(round(x_act[m] . w_in^T + b_in) +
+ * temb[m / rows_per_b]) for rows m < rows: x_act [rows][action_dim]
+ * (action_dim % 8 == 0, <= 64), w_in [d_model][action_dim] (16-byte aligned),
+ * b_in [d_model] or NULL, temb rows of ld_temb elements, x [rows][d_model].
+ * ee_euler_step: x[i] = round(x[i] + round(v[i] * dt)) for i < count and, when
+ * t is not NULL, t[b] = round(t[b] + dt) for b < batch. */
+int ee_time_embed(const void* t, const float* freqs, void* emb, int32_t batch, int32_t dim, int32_t act_dtype,
+                  ee_stream_t stream);
+int ee_expert_head(const void* x_act, const void* w_in, const void* b_in, const void* temb, void* x, int64_t rows,
+                   int32_t action_dim, int32_t d_model, int64_t rows_per_b, int64_t ld_temb, int32_t act_dtype,
+                   ee_stream_t stream);
+int ee_euler_step(void* x, const void* v, void* t, int64_t count, int32_t batch, float dt, int32_t act_dtype,
+                  ee_stream_t stream);
 
 /* ---- fused flow-matching sampler --------------------------------------- */
 typedef struct ee_linear {

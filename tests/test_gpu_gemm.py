@@ -159,6 +159,30 @@ def test_ragged_shapes(cuda, m, n, k, kind):
     assert rel_err(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("m", [33, 50, 64])
+@pytest.mark.parametrize("n,k", [(1000, 128), (136, 384), (4096, 1024), (200, 2048)])
+@pytest.mark.parametrize("kind,group", [("int8", 128), ("int8", "pc"), ("int4", 128), ("int4", 256),
+                                        ("int4z", 128), ("bf16", 0)])
+def test_few_tokens_tensor_core_path(cuda, m, n, k, kind, group):
+    """33-64 tokens (the sampler's 50-token batch among them) run the tcgen05
+    tile kernel with one token tile: one CTA per unit (K = 128, 384: no split)
+    and cluster split-K (K = 1024, 2048), ragged N, per-channel and 256-wide
+    groups, every weight kind, bias + GELU and bias + residual epilogues (f16
+    activations at 33 tokens), against the oracle."""
+    rng = np.random.default_rng(m * 131 + n + k)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    b = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    grp = k if group == "pc" or (group and k % group) else group  # 256-wide groups where K allows
+    y, ref = _run(cuda, x, w, kind, grp, bias=b, gelu=True)
+    assert rel_err(y, ref) <= TOL, (m, n, k, kind, group, rel_err(y, ref))
+    r = rng.standard_normal((m, n)).astype(np.float32)
+    y, ref = _run(cuda, x, w, kind, grp, bias=b, residual=r, act=torch.float16 if m == 33 else torch.bfloat16)
+    assert rel_err(y, ref) <= TOL, (m, n, k, kind, group, rel_err(y, ref))
+    from embodied_efficiency_b200 import wq_gemm
+    assert wq_gemm.gemm_status() == 0
+
+
 @pytest.mark.parametrize("kind", ["int8", "int4", "bf16"])
 def test_epilogues_and_fp16(cuda, kind):
     rng = np.random.default_rng(11)
