@@ -41,41 +41,88 @@ __global__ void __launch_bounds__(kRowThreads) time_embed_kernel(const T* __rest
 }
 
 // x[m][n] = round(round(sum_k x_act[m][k] * W[n][k] + bias[n]) + temb[m / rows_per_b][n]).
-// CTA (x, y) keeps the in_proj weight rows of column slice y, [y * nc, + nc),
-// in shared memory ([nc][A], at most 64 KB) and walks token rows m =
-// blockIdx.x, + gridDim.x, ...; thread j computes columns j, j + 256, ... of
-// the slice.
-template <typename T>
-__global__ void __launch_bounds__(kRowThreads) expert_head_kernel(const T* __restrict__ xa, const T* __restrict__ w,
-                                                                   const T* __restrict__ bias, const T* __restrict__ temb,
-                                                                   T* __restrict__ out, long long rows, int A, int d, int nc,
-                                                                   long long rows_per_b, long long ld_temb) {
-  extern __shared__ __align__(16) char smem[];
-  const int c0 = blockIdx.y * nc, cn = min(nc, d - c0);
-  T* ws = reinterpret_cast<T*>(smem);                                                          // [cn][A]
-  float* xs = reinterpret_cast<float*>(smem + (((size_t)nc * A * 2 + 15) & ~(size_t)15));  // [A]
-  const int chunks = cn * A / 8;
-  const uint4* wsrc = reinterpret_cast<const uint4*>(w + (size_t)c0 * A);
-  for (int i = threadIdx.x; i < chunks; i += kRowThreads) reinterpret_cast<uint4*>(ws)[i] = __ldg(wsrc + i);
-  for (long long m = blockIdx.x; m < rows; m += gridDim.x) {
-    __syncthreads();  // the weights are staged; the previous row's xs is no longer read
-    if (threadIdx.x < A) xs[threadIdx.x] = Act<T>::to_f(xa[m * A + threadIdx.x]);
-    __syncthreads();
-    const T* tr = temb + (m / rows_per_b) * ld_temb;
-    T* orow = out + m * d;
-    for (int j = threadIdx.x; j < cn; j += kRowThreads) {
-      const int n = c0 + j;
-      const T* wr = ws + (size_t)j * A;
-      float acc = 0.f;
-      for (int k = 0; k < A; k += 2) {
-        const float2 f = Act<T>::unpack2(*reinterpret_cast<const uint32_t*>(wr + k));
-        acc = fmaf(xs[k], f.x, acc);
-        acc = fmaf(xs[k + 1], f.y, acc);
-      }
-      acc += bias ? ld_param(bias + n) : 0.f;
-      orow[n] = Act<T>::from_f(Act<T>::round(Act<T>::round(acc) + ld_param(tr + n)));
+// Thread = one output column n (CTA y covers columns [256 y, 256 y + 256)),
+// its AK in_proj weights held in fp32 registers for the whole kernel; the CTA
+// walks batches of kHeadRows token rows (m0 = blockIdx.x * kHeadRows, +
+// gridDim.x * kHeadRows, ...), the batch's activations in shared memory read
+// as broadcast float4s, one fp32 dot product per (row, column) in k order.
+constexpr int kHeadRows = 8;
+template <typename T, int AK>
+__global__ void __launch_bounds__(kRowThreads, 2) expert_head_kernel(const T* __restrict__ xa, const T* __restrict__ w,
+                                                                      const T* __restrict__ bias, const T* __restrict__ temb,
+                                                                      T* __restrict__ out, long long rows, int d,
+                                                                      long long rows_per_b, long long ld_temb) {
+  __shared__ __align__(16) float xs[kHeadRows][AK];
+  __shared__ const T* trow[kHeadRows];  // the batch rows' projected time-embedding rows
+  const int n = blockIdx.y * kRowThreads + threadIdx.x;
+  const bool live = n < d;
+  float wr[AK];
+#pragma unroll
+  for (int c = 0; c < AK / 8; ++c) {
+    const uint4 v = live ? __ldg(reinterpret_cast<const uint4*>(w + (size_t)n * AK) + c) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = Act<T>::unpack2(comp(v, e));
+      wr[8 * c + 2 * e] = f.x;
+      wr[8 * c + 2 * e + 1] = f.y;
     }
   }
+  const float bv = (live && bias) ? ld_param(bias + n) : 0.f;
+  for (long long m0 = (long long)blockIdx.x * kHeadRows; m0 < rows; m0 += (long long)gridDim.x * kHeadRows) {
+    __syncthreads();  // the previous batch's activations are no longer read
+    for (int i = threadIdx.x; i < kHeadRows * AK; i += kRowThreads) {
+      const int r = i / AK, k = i - r * AK;
+      xs[r][k] = m0 + r < rows ? Act<T>::to_f(xa[(m0 + r) * AK + k]) : 0.f;
+    }
+    if (threadIdx.x < kHeadRows) trow[threadIdx.x] = temb + ((m0 + threadIdx.x) / rows_per_b) * ld_temb;
+    __syncthreads();
+#pragma unroll 1
+    for (int r = 0; r < kHeadRows; ++r) {
+      float acc = 0.f;
+#pragma unroll
+      for (int k4 = 0; k4 < AK / 4; ++k4) {
+        const float4 xv = *reinterpret_cast<const float4*>(&xs[r][4 * k4]);
+        acc = fmaf(xv.x, wr[4 * k4], acc);
+        acc = fmaf(xv.y, wr[4 * k4 + 1], acc);
+        acc = fmaf(xv.z, wr[4 * k4 + 2], acc);
+        acc = fmaf(xv.w, wr[4 * k4 + 3], acc);
+      }
+      const long long m = m0 + r;
+      if (live && m < rows)
+        out[m * d + n] = Act<T>::from_f(Act<T>::round(Act<T>::round(acc + bv) + ld_param(trow[r] + n)));
+    }
+  }
+}
+
+template <typename T, int AK>
+static int launch_head(const void* xa, const void* w, const void* b, const void* temb, void* x, long long rows, int d,
+                       long long rows_per_b, long long ld_temb, cudaStream_t s) {
+  const DevProps* dp = device_props();
+  const int slices = (d + kRowThreads - 1) / kRowThreads;
+  const long long batches = (rows + kHeadRows - 1) / kHeadRows;
+  long long gx = (long long)(dp ? dp->sms : 148) * 4 / slices;  // about four CTAs per SM in all
+  if (gx < 1) gx = 1;
+  if (gx > batches) gx = batches;
+  expert_head_kernel<T, AK><<<dim3((unsigned)gx, (unsigned)slices), kRowThreads, 0, s>>>(
+      reinterpret_cast<const T*>(xa), reinterpret_cast<const T*>(w), reinterpret_cast<const T*>(b),
+      reinterpret_cast<const T*>(temb), reinterpret_cast<T*>(x), rows, d, rows_per_b, ld_temb);
+  return cudaGetLastError() == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
+}
+
+template <typename T>
+static int dispatch_head(const void* xa, const void* w, const void* b, const void* temb, void* x, long long rows, int A,
+                         int d, long long rows_per_b, long long ld_temb, cudaStream_t s) {
+  switch (A) {
+    case 8: return launch_head<T, 8>(xa, w, b, temb, x, rows, d, rows_per_b, ld_temb, s);
+    case 16: return launch_head<T, 16>(xa, w, b, temb, x, rows, d, rows_per_b, ld_temb, s);
+    case 24: return launch_head<T, 24>(xa, w, b, temb, x, rows, d, rows_per_b, ld_temb, s);
+    case 32: return launch_head<T, 32>(xa, w, b, temb, x, rows, d, rows_per_b, ld_temb, s);
+    case 40: return launch_head<T, 40>(xa, w, b, temb, x, rows, d, rows_per_b, ld_temb, s);
+    case 48: return launch_head<T, 48>(xa, w, b, temb, x, rows, d, rows_per_b, ld_temb, s);
+    case 56: return launch_head<T, 56>(xa, w, b, temb, x, rows, d, rows_per_b, ld_temb, s);
+    case 64: return launch_head<T, 64>(xa, w, b, temb, x, rows, d, rows_per_b, ld_temb, s);
+  }
+  return EE_ERR_SHAPE;
 }
 
 // x[i] = round(x[i] + round(v[i] * dt)); t[b] = round(t[b] + dt)
@@ -132,36 +179,12 @@ int ee_expert_head(const void* x_act, const void* w_in, const void* b_in, const 
   if (d_model < 8 || rows_per_b < 1 || ld_temb < d_model) return EE_ERR_SHAPE;
   if (!aligned16(w_in)) return EE_ERR_ALIGN;
   if (act_dtype != EE_BF16 && act_dtype != EE_F16) return EE_ERR_DTYPE;
-  // column slices of at most 64 KB of weights (a multiple of 256 columns)
-  int nc = (int)((65536 / (action_dim * 2)) / kRowThreads * kRowThreads);
-  if (nc > d_model) nc = d_model;
-  const int slices = (d_model + nc - 1) / nc;
-  const size_t smem = (((size_t)nc * action_dim * 2 + 15) & ~(size_t)15) + (size_t)kHeadMaxA * 4;
   const int rc = check_device();
   if (rc) return rc;
   cudaStream_t s = (cudaStream_t)stream;
-  unsigned gx = grid_for(rows, 8);
-  gx = gx / (unsigned)slices > 0 ? gx / (unsigned)slices : 1;
-  const dim3 grid(gx, (unsigned)slices);
-  if (act_dtype == EE_BF16) {
-    auto fn = expert_head_kernel<__nv_bfloat16>;
-    static std::atomic<int> set[64];
-    allow_max_smem(fn, set);
-    fn<<<grid, kRowThreads, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(x_act),
-                                       reinterpret_cast<const __nv_bfloat16*>(w_in),
-                                       reinterpret_cast<const __nv_bfloat16*>(b_in),
-                                       reinterpret_cast<const __nv_bfloat16*>(temb),
-                                       reinterpret_cast<__nv_bfloat16*>(x), rows, action_dim, d_model, nc, rows_per_b,
-                                       ld_temb);
-  } else {
-    auto fn = expert_head_kernel<__half>;
-    static std::atomic<int> set[64];
-    allow_max_smem(fn, set);
-    fn<<<grid, kRowThreads, smem, s>>>(reinterpret_cast<const __half*>(x_act), reinterpret_cast<const __half*>(w_in),
-                                       reinterpret_cast<const __half*>(b_in), reinterpret_cast<const __half*>(temb),
-                                       reinterpret_cast<__half*>(x), rows, action_dim, d_model, nc, rows_per_b, ld_temb);
-  }
-  return cudaGetLastError() == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
+  if (act_dtype == EE_BF16)
+    return dispatch_head<__nv_bfloat16>(x_act, w_in, b_in, temb, x, rows, action_dim, d_model, rows_per_b, ld_temb, s);
+  return dispatch_head<__half>(x_act, w_in, b_in, temb, x, rows, action_dim, d_model, rows_per_b, ld_temb, s);
 }
 
 int ee_euler_step(void* x, const void* v, void* t, int64_t count, int32_t batch, float dt, int32_t act_dtype,
