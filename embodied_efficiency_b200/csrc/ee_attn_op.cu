@@ -38,6 +38,7 @@ struct StreamSmem {
 template <typename T, int HD>
 __global__ void __launch_bounds__(kThreads) attention_kernel(const __grid_constant__ AttnArgs a, int units) {
   extern __shared__ __align__(128) char smem[];
+  pdl_entry();
   for (int u = blockIdx.x; u < units; u += gridDim.x) Attn<T, HD>::unit(a, u / a.n_heads, u % a.n_heads, smem);
 }
 
@@ -45,6 +46,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const __grid_consta
 template <typename T, int HD>
 __global__ void __launch_bounds__(kThreads) attention_pair_kernel(const __grid_constant__ AttnArgs a, int units) {
   extern __shared__ __align__(128) char smem[];
+  pdl_entry();
   using U = Attn<T, HD>;
   using S = AttnSmem<HD>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -114,8 +116,7 @@ static int launch_attention(const AttnArgs& a, int units, cudaStream_t s) {
   per_sm = per_sm < 1 ? 1 : (per_sm > 4 ? 4 : per_sm);
   const long long cap = (long long)dp->sms * per_sm;
   const int grid = (int)(units < cap ? units : cap);
-  fn<<<grid, kThreads, smem, s>>>(a, units);
-  return cudaGetLastError() == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
+  return launch_pdl(fn, dim3(grid), dim3(kThreads), (size_t)smem, s, a, units) == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
 }
 
 }  // namespace ee

@@ -240,6 +240,18 @@ EE_DEV uint32_t cl_count() {
   asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
   return r;
 }
+#ifndef EE_PDL
+#define EE_PDL 1
+#endif
+// Kernel entry under programmatic dependent launch (see ee_host.h): wait for
+// the predecessor grids (complete, memory visible), then allow the successor
+// to launch. A no-op for kernels launched without the attribute.
+EE_DEV void pdl_entry() {
+#if EE_PDL
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
+}
 EE_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }

@@ -9,9 +9,45 @@
 
 #include "../../include/ee_b200.h"
 
+// Programmatic dependent launch of the standalone kernels (GEMMs, norm,
+// attention, row operations): each is launched with programmatic stream
+// serialization and, first thing, waits for its predecessors
+// (griddepcontrol.wait) and then lets its successor launch
+// (griddepcontrol.launch_dependents), so a successor's launch and CTA
+// scheduling overlap this kernel's run while its memory accesses still come
+// after this kernel completes. The fused sampler is launched without it.
+#ifndef EE_PDL
+#define EE_PDL 1
+#endif
+
 namespace ee {
 
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// append the programmatic-serialization attribute (with EE_PDL) to a launch's list
+inline void add_pdl_attr(cudaLaunchAttribute* attrs, unsigned int& n) {
+  if (EE_PDL) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+}
+
+// a plain launch (no cluster) with the programmatic-serialization attribute
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  unsigned int n = 0;
+  add_pdl_attr(attr, n);
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, fn, args...);
+}
 
 struct DevProps {
   int sms;        // multiprocessor count

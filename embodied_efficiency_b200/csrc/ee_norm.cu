@@ -26,6 +26,7 @@ __global__ void __launch_bounds__(kNormWarps * 32) layer_norm_kernel(const T* __
                                                                       const T* __restrict__ b, T* __restrict__ y,
                                                                       long long rows, int cols, long long ldx,
                                                                       long long ldy, float eps) {
+  pdl_entry();
   const int lane = threadIdx.x & 31;
   const long long stride = (long long)gridDim.x * kNormWarps;
   long long row = (long long)blockIdx.x * kNormWarps + (threadIdx.x >> 5);
@@ -111,8 +112,10 @@ static int launch_norm(const T* x, const T* w, const T* b, T* y, long long rows,
   const long long need = (rows + kNormWarps - 1) / kNormWarps;
   const long long cap = (long long)dp->sms * per_sm;
   const unsigned grid = (unsigned)(need < cap ? need : cap);
-  layer_norm_kernel<T, NCH><<<grid, kNormWarps * 32, 0, s>>>(x, w, b, y, rows, cols, ldx, ldy, eps);
-  return cudaGetLastError() == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
+  return launch_pdl(layer_norm_kernel<T, NCH>, dim3(grid), dim3(kNormWarps * 32), 0, s, x, w, b, y, rows, cols, ldx, ldy,
+                    eps) == cudaSuccess
+             ? EE_OK
+             : EE_ERR_LAUNCH;
 }
 
 template <typename T>

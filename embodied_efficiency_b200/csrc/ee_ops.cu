@@ -38,6 +38,7 @@ template <typename T, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     wq_gemm_kernel(const __grid_constant__ GemmArgs a, GemmSmem sm) {
   extern __shared__ __align__(128) char smem[];
+  pdl_entry();
   Gemm<T, KIND>::run(a, smem, sm, nullptr);
 }
 

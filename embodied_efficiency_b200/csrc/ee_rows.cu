@@ -30,6 +30,7 @@ constexpr int kHeadMaxA = 64;  // action_dim bound of ee_expert_head
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads) time_embed_kernel(const T* __restrict__ t, const float* __restrict__ freqs,
                                                                   T* __restrict__ emb, int batch, int half) {
+  pdl_entry();
   const long long total = (long long)batch * half;
   for (long long idx = (long long)blockIdx.x * kRowThreads + threadIdx.x; idx < total;
        idx += (long long)gridDim.x * kRowThreads) {
@@ -52,6 +53,7 @@ __global__ void __launch_bounds__(kRowThreads, 2) expert_head_kernel(const T* __
                                                                       const T* __restrict__ bias, const T* __restrict__ temb,
                                                                       T* __restrict__ out, long long rows, int d,
                                                                       long long rows_per_b, long long ld_temb) {
+  pdl_entry();
   __shared__ __align__(16) float xs[kHeadRows][AK];
   __shared__ const T* trow[kHeadRows];  // the batch rows' projected time-embedding rows
   const int n = blockIdx.y * kRowThreads + threadIdx.x;
@@ -103,10 +105,11 @@ static int launch_head(const void* xa, const void* w, const void* b, const void*
   long long gx = (long long)(dp ? dp->sms : 148) * 4 / slices;  // about four CTAs per SM in all
   if (gx < 1) gx = 1;
   if (gx > batches) gx = batches;
-  expert_head_kernel<T, AK><<<dim3((unsigned)gx, (unsigned)slices), kRowThreads, 0, s>>>(
-      reinterpret_cast<const T*>(xa), reinterpret_cast<const T*>(w), reinterpret_cast<const T*>(b),
-      reinterpret_cast<const T*>(temb), reinterpret_cast<T*>(x), rows, d, rows_per_b, ld_temb);
-  return cudaGetLastError() == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
+  return launch_pdl(expert_head_kernel<T, AK>, dim3((unsigned)gx, (unsigned)slices), dim3(kRowThreads), 0, s,
+                    reinterpret_cast<const T*>(xa), reinterpret_cast<const T*>(w), reinterpret_cast<const T*>(b),
+                    reinterpret_cast<const T*>(temb), reinterpret_cast<T*>(x), rows, d, rows_per_b, ld_temb) == cudaSuccess
+             ? EE_OK
+             : EE_ERR_LAUNCH;
 }
 
 template <typename T>
@@ -129,6 +132,7 @@ static int dispatch_head(const void* xa, const void* w, const void* b, const voi
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads) euler_step_kernel(T* __restrict__ x, const T* __restrict__ v, T* __restrict__ t,
                                                                   long long count, int batch, float dt) {
+  pdl_entry();
   for (long long i = (long long)blockIdx.x * kRowThreads + threadIdx.x; i < count;
        i += (long long)gridDim.x * kRowThreads)
     x[i] = Act<T>::from_f(Act<T>::round(Act<T>::to_f(x[i]) + Act<T>::round(Act<T>::to_f(v[i]) * dt)));
@@ -161,13 +165,13 @@ int ee_time_embed(const void* t, const float* freqs, void* emb, int32_t batch, i
   cudaStream_t s = (cudaStream_t)stream;
   const int half = dim / 2;
   const unsigned grid = grid_for((long long)batch * half, kRowThreads);
-  if (act_dtype == EE_BF16)
-    time_embed_kernel<__nv_bfloat16><<<grid, kRowThreads, 0, s>>>(
-        reinterpret_cast<const __nv_bfloat16*>(t), freqs, reinterpret_cast<__nv_bfloat16*>(emb), batch, half);
-  else
-    time_embed_kernel<__half><<<grid, kRowThreads, 0, s>>>(reinterpret_cast<const __half*>(t), freqs,
-                                                           reinterpret_cast<__half*>(emb), batch, half);
-  return cudaGetLastError() == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
+  const cudaError_t e =
+      act_dtype == EE_BF16
+          ? launch_pdl(time_embed_kernel<__nv_bfloat16>, dim3(grid), dim3(kRowThreads), 0, s,
+                       reinterpret_cast<const __nv_bfloat16*>(t), freqs, reinterpret_cast<__nv_bfloat16*>(emb), batch, half)
+          : launch_pdl(time_embed_kernel<__half>, dim3(grid), dim3(kRowThreads), 0, s, reinterpret_cast<const __half*>(t),
+                       freqs, reinterpret_cast<__half*>(emb), batch, half);
+  return e == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
 }
 
 int ee_expert_head(const void* x_act, const void* w_in, const void* b_in, const void* temb, void* x, int64_t rows,
@@ -196,14 +200,14 @@ int ee_euler_step(void* x, const void* v, void* t, int64_t count, int32_t batch,
   if (rc) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   const unsigned grid = grid_for(count, kRowThreads * 4);
-  if (act_dtype == EE_BF16)
-    euler_step_kernel<__nv_bfloat16><<<grid, kRowThreads, 0, s>>>(
-        reinterpret_cast<__nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(v),
-        reinterpret_cast<__nv_bfloat16*>(t), count, batch, dt);
-  else
-    euler_step_kernel<__half><<<grid, kRowThreads, 0, s>>>(reinterpret_cast<__half*>(x), reinterpret_cast<const __half*>(v),
-                                                           reinterpret_cast<__half*>(t), count, batch, dt);
-  return cudaGetLastError() == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
+  const cudaError_t e =
+      act_dtype == EE_BF16
+          ? launch_pdl(euler_step_kernel<__nv_bfloat16>, dim3(grid), dim3(kRowThreads), 0, s,
+                       reinterpret_cast<__nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(v),
+                       reinterpret_cast<__nv_bfloat16*>(t), count, batch, dt)
+          : launch_pdl(euler_step_kernel<__half>, dim3(grid), dim3(kRowThreads), 0, s, reinterpret_cast<__half*>(x),
+                       reinterpret_cast<const __half*>(v), reinterpret_cast<__half*>(t), count, batch, dt);
+  return e == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
 }
 
 }  // extern "C"

@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const uint32_t base0 = smem_u32(smem_raw);
   const uint32_t sb = (base0 + 1023u) & ~1023u;
   char* smem = smem_raw + (sb - base0);
+  pdl_entry();
 
   const int S = 1 << a.lsplit;
   if ((int)cl_size() != S) {  // launched without the planned cluster: no work
@@ -486,13 +487,15 @@ int stream_launch_k(const GemmArgs& g, int* status, cudaStream_t st, bool* used)
   cfg.blockDim = dim3(kStreamThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = S;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  unsigned int nattr = 1;
+  add_pdl_attr(attr, nattr);
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = nattr;
   *used = true;
   return cudaLaunchKernelEx(&cfg, fn, tw, tx, a) == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
 }

@@ -174,6 +174,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t base0 = smem_u32(smem_raw);
   const uint32_t sb = (base0 + 1023u) & ~1023u;
   char* smem = smem_raw + (sb - base0);
+  pdl_entry();
 
   const int S = 1 << a.lsplit;
   if ((int)cl_size() != S) {
@@ -624,6 +625,11 @@ int tc_launch_k(const GemmArgs& g, const TcShape& sh, int* status, cudaStream_t 
     cfg.blockDim = dim3(kTcpThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
+    cudaLaunchAttribute pattr[1];
+    unsigned int npattr = 0;
+    add_pdl_attr(pattr, npattr);
+    cfg.attrs = pattr;
+    cfg.numAttrs = npattr;
     *used = true;
     return cudaLaunchKernelEx(&cfg, fnp, tw, tx, a) == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
   }
@@ -637,13 +643,15 @@ int tc_launch_k(const GemmArgs& g, const TcShape& sh, int* status, cudaStream_t 
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = S;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  unsigned int nattr = 1;
+  add_pdl_attr(attr, nattr);
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = nattr;
   *used = true;
   return cudaLaunchKernelEx(&cfg, fn, tw, tx, a) == cudaSuccess ? EE_OK : EE_ERR_LAUNCH;
 }

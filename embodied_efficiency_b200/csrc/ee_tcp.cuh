@@ -46,6 +46,7 @@ __global__ void __launch_bounds__(kTcpThreads, 1)
   const uint32_t base0 = smem_u32(smem_raw);
   const uint32_t sb = (base0 + 1023u) & ~1023u;
   char* smem = smem_raw + (sb - base0);
+  pdl_entry();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = a.n_units * ((a.M + NT - 1) / NT);
