@@ -342,6 +342,30 @@ def fleet_run(expert, rank, world, dev, n_requests=256, chunk=256, steps=5, warm
             "scaling": "strong (fixed 256 requests split over the GPUs)", "collectives": "none on the data path"}
 
 
+def fleet_share_run(expert, world, dev, n_requests=256, chunk=256, steps=5, warmup=3):
+    """Rank 0's share of the fleet for a world of `world` GPUs, timed on this
+    one GPU. Fleet mode has no collective, so a rank's fleet step is its own
+    work; the aggregate it projects for `world` GPUs is n_requests * horizon /
+    (rank 0's step time), rank 0 holding the largest share."""
+    from embodied_efficiency_b200 import synth
+    from embodied_efficiency_b200.fleet import FleetSampler
+    cfg = expert.cfg
+    fs = FleetSampler(n_requests, 0, world, chunk=chunk, expert=expert, device=dev)
+    fs.stage(lambda i: synth.fleet_request(cfg, i))
+    for _ in range(warmup):
+        fs.run_device()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fs.run_device()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"world": world, "requests_per_gpu": fs.hi - fs.lo, "ms_per_fleet_step": round(ms, 3),
+            "projected_actions_per_s": round(n_requests * cfg.horizon / (ms * 1e-3), 1)}
+
+
 def cpu_baseline_run(budget_s=15.0, bits=4):
     """The oracle (CPU restatement of the reference path) on the host cores."""
     from embodied_efficiency_b200 import synth
@@ -414,7 +438,9 @@ def profile_case(spec, launches):
     queries, 16 heads of 64, P prefix keys), ``selfattn:BATCH`` its
     self-attention over the 50 action tokens (q / k / v read in place from the
     fused projection) and ``dequant:N:K:BITS`` the weight dequantisation
-    kernel on an [N, K] weight (group 128)."""
+    kernel on an [N, K] weight (group 128), ``fleet:WORLD`` rank 0's share of
+    the 256-request int4 fleet for WORLD GPUs (its fleet steps after two
+    warm-up steps)."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     kind, *rest = spec.split(":")
@@ -506,6 +532,17 @@ def profile_case(spec, launches):
             y = dequant_weight(wt, sc, 128, bits, torch.bfloat16)
         torch.cuda.synchronize()
         print(f"dequant n={n} k={k} bits={bits} mean|w|={float(y.float().abs().mean()):.6f}")
+    elif kind == "fleet":
+        from embodied_efficiency_b200 import synth
+        from embodied_efficiency_b200.fleet import FleetSampler
+        world = int(rest[0]) if rest else 8
+        m, x0, prefix = build_expert(4, dev)
+        fs = FleetSampler(256, 0, world, chunk=256, expert=m, device=dev)
+        fs.stage(lambda i: synth.fleet_request(m.cfg, i))
+        for _ in range(2 + launches):
+            fs.run_device()
+        torch.cuda.synchronize()
+        print(f"fleet world={world} requests={fs.hi - fs.lo}")
     else:
         raise SystemExit(f"unknown --profile case {spec!r}")
 
@@ -521,12 +558,24 @@ def main():
     ap.add_argument("--no-fleet", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the config 3-ref and config 5 sampler lines")
     ap.add_argument("--fleet-chunk", type=int, default=256)
+    ap.add_argument("--fleet-share", default=None,
+                    help="comma-separated world sizes: time rank 0's fleet share for each on this GPU and print "
+                         "the projected aggregate (one JSON line), nothing else")
     ap.add_argument("--profile", default=None,
                     help="gemm:M:K:BITS[:N[:gelu]], sampler:BITS, norm:ROWS:COLS, attn:BATCH:P, selfattn:BATCH or dequant:N:K:BITS -- a few launches for a profiler")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.profile:
         return profile_case(args.profile, max(args.steps if args.steps != 200 else 4, 1))
+    if args.fleet_share:
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        m, _, _ = build_expert(4, dev)
+        shares = [fleet_share_run(m, int(w), dev) for w in args.fleet_share.split(",")]
+        print(json.dumps({"metric": "projected fleet actions/s (rank 0's share timed on one GPU)",
+                          "workload": "256 requests x (10-step int4 group-128 sampler, d1024 L4, own prefix and noise)",
+                          "shares": shares}))
+        return
     if args.impl == "reference":
         return run_reference(args)
 
